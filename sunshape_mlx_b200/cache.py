@@ -1,0 +1,601 @@
+"""SunShape KV caches resident in GPU memory (cache.py of the reference).
+
+Layouts (all contiguous, per (batch, kv-head) pair a fixed-capacity stream):
+  key indices   (B, H, cap, n_blocks) uint8
+  heavy keys    (B, H, cap, n_heavy * block_dim) fp16   (mixed-precision codec)
+  fp16 values   (B, H, cap, D) fp16
+  grouped       packed (B, H, cap, words) + scales/zeros (B, H, cap, G) f32
+  turboquant    packed (B, H, cap, words) + norms (B, H, cap) f32
+                (or per-group fp16 scales (B, H, cap, G) in the grouped variant)
+  hybrid tail   fp16 keys/values (B, H, bufcap, D) in the original basis
+Capacities grow in 256-token steps (cache.py:33) and tails in 128-token
+multiples, so every stream holds whole tiles of the fused attention kernel.
+Appends quantize keys and encode values directly into the cache slices.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import kernels as K
+from .codec import SunShapeBlockCodec
+from .value_codecs import GroupedValueCodec, TurboQuantValueCodec, build_value_codec
+
+__all__ = ["SunShapeKVCache", "HybridSunShapeKVCache", "create_kv_cache"]
+
+_STEP = 256
+_DEFAULT_BUFFER_SIZE = 128
+_TAIL_STEP = 128
+
+
+def _round_up(x: int, m: int) -> int:
+    return ((x + m - 1) // m) * m
+
+
+def _grow(old: torch.Tensor | None, shape: tuple, used: int, dtype, device, fill_zero=True):
+    """New buffer of `shape`; copies old[:, :, :used] over."""
+    new = (torch.zeros if fill_zero else torch.empty)(shape, dtype=dtype, device=device)
+    if old is not None and used > 0:
+        new[:, :, :used] = old[:, :, :used]
+    return new
+
+
+def _causal_mask(offset: int, n: int, return_array: bool):
+    """mlx-lm style mask for n new queries at positions [offset, offset+n)."""
+    if offset == 0 and n == 0:
+        return "none"
+    if not return_array:
+        return "causal"
+    qpos = torch.arange(offset, offset + n)
+    kpos = torch.arange(offset + n)
+    ok = qpos[:, None] >= kpos[None, :]
+    return torch.where(ok, torch.tensor(0.0), torch.tensor(torch.finfo(torch.float16).min)).to(
+        torch.float16)
+
+
+class SunShapeKVCache:
+    """Keys as block-VQ indices + fp16 values (cache.py:59-336)."""
+
+    def __init__(self, codec: SunShapeBlockCodec, *, n_kv_heads: int = 1,
+                 head_dim: int | None = None, dtype=torch.float16):
+        self.codec = codec
+        self.device = codec.device
+        self.n_kv_heads = n_kv_heads
+        self.head_dim = head_dim or codec.head_dim
+        self.block_dim = codec.block_dim
+        self.n_blocks = codec.n_blocks
+        self.n_centroids = codec.n_centroids
+        self.dtype = dtype
+        self.offset = 0
+        self._key_indices = None
+        self._key_heavy = None
+        self._values = None
+        self._capacity = 0
+        self._batch = 0
+
+    # ------------------------------------------------------------ storage
+    def _ensure_capacity(self, B: int, new_tokens: int) -> None:
+        """cache.py:102-150: grow to a multiple of 256 tokens."""
+        need = self.offset + new_tokens
+        if self._key_indices is not None and B != self._batch:
+            raise ValueError(f"batch size changed from {self._batch} to {B}")
+        if need <= self._capacity:
+            return
+        cap = _round_up(need, _STEP)
+        H, dev = self.n_kv_heads, self.device
+        self._key_indices = _grow(self._key_indices, (B, H, cap, self.n_blocks), self.offset,
+                                  torch.uint8, dev)
+        self._values = _grow(self._values, (B, H, cap, self.head_dim), self.offset,
+                             torch.float16, dev)
+        nh = self.codec.n_heavy_blocks
+        if nh:
+            self._key_heavy = _grow(self._key_heavy, (B, H, cap, nh * self.block_dim),
+                                    self.offset, torch.float16, dev)
+        self._capacity = cap
+        self._batch = B
+
+    def append(self, keys, values) -> None:
+        """Quantize and store new tokens without materialising anything
+        (the write half of update_and_fetch)."""
+        k = K.cuda_tensor(keys, device=self.device)
+        v = K.cuda_tensor(values, device=self.device)
+        B, H, T, D = k.shape
+        if H != self.n_kv_heads:
+            raise AssertionError(f"Expected {self.n_kv_heads} kv heads, got {H}")
+        if D != self.head_dim:
+            raise AssertionError(f"Expected head_dim {self.head_dim}, got {D}")
+        if T == 0:
+            return
+        self._ensure_capacity(B, T)
+        o = self.offset
+        _quantize_keys_into(self.codec, k, self._key_indices[:, :, o:o + T],
+                            None if self._key_heavy is None else self._key_heavy[:, :, o:o + T])
+        self._values[:, :, o:o + T] = v
+        self.offset += T
+
+    def update_and_fetch(self, keys, values):
+        """cache.py:156-205: append, then return (keys, values) as stored
+        (keys dequantized); the fused SDPA does not use the returned keys."""
+        self.append(keys, values)
+        return self.keys, self.values
+
+    # ------------------------------------------------------------ views
+    @property
+    def keys(self) -> torch.Tensor:
+        """Dequantized keys (B, H, T, D) float32 (cache.py:211-240)."""
+        if self._key_indices is None or self.offset == 0:
+            return torch.zeros((1, self.n_kv_heads, 0, self.head_dim), dtype=torch.float32,
+                               device=self.device)
+        return _dequantize_keys(self.codec, self._key_indices[:, :, :self.offset],
+                                None if self._key_heavy is None else self._key_heavy[:, :, :self.offset])
+
+    @property
+    def values(self) -> torch.Tensor:
+        if self._values is None or self.offset == 0:
+            return torch.zeros((1, self.n_kv_heads, 0, self.head_dim), dtype=self.dtype,
+                               device=self.device)
+        return self._values[:, :, :self.offset]
+
+    @property
+    def key_indices(self) -> torch.Tensor:
+        if self._key_indices is None or self.offset == 0:
+            return torch.zeros((1, self.n_kv_heads, 0, self.n_blocks), dtype=torch.uint8,
+                               device=self.device)
+        return self._key_indices[:, :, :self.offset]
+
+    @property
+    def state(self):
+        return (self.key_indices, self.values)
+
+    # ------------------------------------------------------------ fused-attention view
+    def attention_spec(self) -> dict:
+        cap = self._capacity
+        spec = dict(tc=self.offset, cap=cap, idx=self._key_indices, v=self._values)
+        if self._key_heavy is not None:
+            spec["kheavy"] = self._key_heavy
+        return spec
+
+    # ------------------------------------------------------------ accounting
+    @property
+    def nbytes(self) -> int:
+        if self._key_indices is None:
+            return 0
+        B, T = self._batch, self.offset
+        nh = self.codec.n_heavy_blocks
+        return (B * self.n_kv_heads * T * self.n_blocks + B * self.n_kv_heads * T * self.head_dim * 2
+                + B * self.n_kv_heads * T * nh * self.block_dim * 2)
+
+    @property
+    def nbytes_equivalent_fp16(self) -> int:
+        if self.offset == 0:
+            return 0
+        B = self._batch or 1
+        return 2 * B * self.n_kv_heads * self.offset * self.head_dim * 2
+
+    @property
+    def compression_ratio(self) -> float:
+        fp16 = self.nbytes_equivalent_fp16
+        return 1.0 if fp16 == 0 else fp16 / max(1, self.nbytes)
+
+    def is_trimmable(self) -> bool:
+        return True
+
+    def trim(self, n: int) -> None:
+        self.offset = max(0, self.offset - n)
+
+    def empty(self) -> bool:
+        return self.offset == 0
+
+    def make_mask(self, N: int, return_array: bool = False, window_size=None, **kwargs):
+        return _causal_mask(self.offset, N, return_array)
+
+    def __repr__(self) -> str:
+        return (f"SunShapeKVCache(offset={self.offset}, head_dim={self.head_dim}, "
+                f"n_blocks={self.n_blocks}, n_centroids={self.n_centroids}, "
+                f"compression={self.compression_ratio:.1f}x)")
+
+
+def _quantize_keys_into(codec: SunShapeBlockCodec, keys: torch.Tensor, idx_out: torch.Tensor,
+                        heavy_out: torch.Tensor | None) -> None:
+    """Assigns (B, H, T, D) keys straight into a strided cache slice."""
+    if codec.use_rotation:
+        from .rotation import _matmul_f32
+        keys = _matmul_f32(keys.float(), codec.rotation.T).contiguous()
+        perm = None
+    else:
+        perm = codec.permutation if codec._is_perm() else None
+    B, H, T, D = keys.shape
+    K.vq_assign(keys.reshape(B * H, T, D), codec.centroids, perm=perm, heavy=codec.heavy_u8,
+                out_idx=idx_out.reshape(B * H, T, -1) if _viewable(idx_out) else idx_out,
+                out_heavy=None if heavy_out is None else heavy_out.reshape(B * H, T, -1))
+
+
+def _viewable(t: torch.Tensor) -> bool:
+    return t.stride(0) == t.stride(1) * t.shape[1]
+
+
+def _dequantize_keys(codec: SunShapeBlockCodec, idx: torch.Tensor,
+                     heavy_vals: torch.Tensor | None) -> torch.Tensor:
+    inv = codec.inv_permutation if codec._is_perm() else None
+    out = K.vq_dequant(idx, codec.centroids, inv_perm=inv,
+                       heavy=codec.heavy_u8 if heavy_vals is not None else None,
+                       heavy_vals=heavy_vals)
+    if codec.use_rotation:
+        from .rotation import _matmul_f32
+        out = _matmul_f32(out, codec.rotation)
+    return out
+
+
+class HybridSunShapeKVCache:
+    """fp16 recent-token buffer + compressed tail (cache.py:348-998)."""
+
+    def __init__(self, codec: SunShapeBlockCodec, *, n_kv_heads: int = 1,
+                 head_dim: int | None = None, dtype=torch.float16,
+                 buffer_size: int = _DEFAULT_BUFFER_SIZE, value_backend: str | None = None,
+                 value_bits: int | None = None, value_group_size: int = 64, value_seed: int = 43,
+                 value_codec: SunShapeBlockCodec | None = None, prefer_metal_kernels: bool = True,
+                 tq_group_size: int | None = None, value_rotation=None):
+        self.codec = codec
+        self.device = codec.device
+        self.n_kv_heads = n_kv_heads
+        self.head_dim = head_dim or codec.head_dim
+        self.block_dim = codec.block_dim
+        self.n_blocks = codec.n_blocks
+        self.n_centroids = codec.n_centroids
+        self.dtype = dtype
+        self.buffer_size = buffer_size
+        self.value_backend = value_backend or ("fp16" if value_bits is None else "grouped")
+        self.value_bits = value_bits
+        self.value_group_size = value_group_size
+        self.value_seed = value_seed
+        self.prefer_metal_kernels = prefer_metal_kernels
+        self.value_codec = value_codec
+        self.last_value_quant_backend = "none"
+        if self.value_backend not in {"fp16", "grouped", "turboquant", "sunshape"}:
+            raise ValueError(f"Unsupported value backend: {self.value_backend}")
+        if self.value_backend != "fp16" and self.value_bits is None:
+            raise ValueError(f"value_bits is required for value backend {self.value_backend}")
+        if self.value_backend == "grouped" and self.head_dim % self.value_group_size != 0:
+            raise ValueError(
+                f"head_dim ({self.head_dim}) must be divisible by "
+                f"value_group_size ({self.value_group_size}) for value quantization")
+        if self.value_backend == "sunshape":
+            self.value_codec = self.value_codec or codec
+            if self.value_codec.head_dim != self.head_dim:
+                raise ValueError("SunShape value codec head_dim must match cache head_dim")
+            self.value_n_blocks = self.value_codec.n_blocks
+            self.value_n_centroids = self.value_codec.n_centroids
+        else:
+            self.value_n_blocks = 0
+            self.value_n_centroids = 0
+        self._value_codec_impl = None
+        if self.value_backend in ("grouped", "turboquant"):
+            self._value_codec_impl = build_value_codec(
+                self.value_backend, head_dim=self.head_dim, value_bits=self.value_bits or 0,
+                value_group_size=self.value_group_size, value_seed=self.value_seed,
+                prefer_metal=prefer_metal_kernels, tq_group_size=tq_group_size,
+                device=self.device)
+            if value_rotation is not None and self.value_backend == "turboquant":
+                c = self._value_codec_impl
+                c.rotation = K.cuda_tensor(value_rotation, torch.float32, self.device)
+                c.rotation_t = c.rotation.T.contiguous()
+        self._compressed_offset = 0
+        self._buffer_offset = 0
+        self._batch = 0
+        self._key_buffer = None
+        self._value_buffer = None
+        self._key_indices = None
+        self._key_heavy = None
+        self._values_packed = None
+        self._value_scales = None
+        self._value_zeros = None
+        self._value_norms = None
+        self._value_indices = None
+        self._values_fp16 = None
+        self._compressed_capacity = 0
+
+    @property
+    def offset(self) -> int:
+        return self._compressed_offset + self._buffer_offset
+
+    # ------------------------------------------------------------ append / flush
+    def _ensure_compressed(self, B: int, n: int) -> None:
+        need = self._compressed_offset + n
+        if need <= self._compressed_capacity:
+            return
+        cap = _round_up(need, _STEP)
+        H, dev, u = self.n_kv_heads, self.device, self._compressed_offset
+        self._key_indices = _grow(self._key_indices, (B, H, cap, self.n_blocks), u, torch.uint8, dev)
+        nh = self.codec.n_heavy_blocks
+        if nh:
+            self._key_heavy = _grow(self._key_heavy, (B, H, cap, nh * self.block_dim), u,
+                                    torch.float16, dev)
+        vc = self._value_codec_impl
+        if self.value_backend == "grouped":
+            self._values_packed = _grow(self._values_packed, (B, H, cap, vc.packed_dim), u, torch.int32, dev)
+            self._value_scales = _grow(self._value_scales, (B, H, cap, vc.n_groups), u, torch.float32, dev)
+            self._value_zeros = _grow(self._value_zeros, (B, H, cap, vc.n_groups), u, torch.float32, dev)
+        elif self.value_backend == "turboquant":
+            self._values_packed = _grow(self._values_packed, (B, H, cap, vc.packed_dim), u, torch.int32, dev)
+            if vc.group_size is None:
+                self._value_norms = _grow(self._value_norms, (B, H, cap), u, torch.float32, dev)
+            else:
+                self._value_norms = _grow(self._value_norms, (B, H, cap, vc.n_scale_groups), u,
+                                          torch.float16, dev)
+        elif self.value_backend == "sunshape":
+            self._value_indices = _grow(self._value_indices, (B, H, cap, self.value_n_blocks), u,
+                                        torch.uint8, dev)
+        else:
+            self._values_fp16 = _grow(self._values_fp16, (B, H, cap, self.head_dim), u,
+                                      torch.float16, dev)
+        self._compressed_capacity = cap
+
+    def _flush_buffer(self, B: int, n: int) -> None:
+        """Moves the oldest n buffered tokens to compressed storage (cache.py:463-650)."""
+        n = min(n, self._buffer_offset)
+        if n <= 0:
+            return
+        self._ensure_compressed(B, n)
+        c0 = self._compressed_offset
+        kf = self._key_buffer[:, :, :n]
+        vf = self._value_buffer[:, :, :n]
+        _quantize_keys_into(self.codec, kf, self._key_indices[:, :, c0:c0 + n],
+                            None if self._key_heavy is None else self._key_heavy[:, :, c0:c0 + n])
+        vc = self._value_codec_impl
+        if self.value_backend == "grouped":
+            vc.quantize_into(vf, self._values_packed[:, :, c0:c0 + n],
+                             self._value_scales[:, :, c0:c0 + n], self._value_zeros[:, :, c0:c0 + n])
+            self.last_value_quant_backend = vc.last_quantize_backend
+        elif self.value_backend == "turboquant":
+            vc.quantize_into(vf, self._values_packed[:, :, c0:c0 + n], self._value_norms[:, :, c0:c0 + n])
+            self.last_value_quant_backend = vc.last_quantize_backend
+        elif self.value_backend == "sunshape":
+            _quantize_keys_into(self.value_codec, vf, self._value_indices[:, :, c0:c0 + n], None)
+            self.last_value_quant_backend = "sunshape"
+        else:
+            self._values_fp16[:, :, c0:c0 + n] = vf
+            self.last_value_quant_backend = "fp16"
+        rem = self._buffer_offset - n
+        if rem > 0:
+            self._key_buffer[:, :, :rem] = self._key_buffer[:, :, n:n + rem].clone()
+            self._value_buffer[:, :, :rem] = self._value_buffer[:, :, n:n + rem].clone()
+        self._compressed_offset += n
+        self._buffer_offset = rem
+
+    def append(self, keys, values) -> None:
+        """Append to the fp16 buffer and flush overflow (cache.py:656-710)."""
+        k = K.cuda_tensor(keys, device=self.device)
+        v = K.cuda_tensor(values, device=self.device)
+        B, H, T, D = k.shape
+        if H != self.n_kv_heads or D != self.head_dim:
+            raise AssertionError("kv heads / head_dim mismatch")
+        if self._batch and B != self._batch:
+            raise ValueError(f"batch size changed from {self._batch} to {B}")
+        self._batch = B
+        need = self._buffer_offset + T
+        cur = 0 if self._key_buffer is None else self._key_buffer.shape[2]
+        if need > cur:
+            size = _round_up(max(self.buffer_size, need, 2 * cur if cur else 0, 1), _TAIL_STEP)
+            self._key_buffer = _grow(self._key_buffer, (B, H, size, D), self._buffer_offset,
+                                     torch.float16, self.device)
+            self._value_buffer = _grow(self._value_buffer, (B, H, size, D), self._buffer_offset,
+                                       torch.float16, self.device)
+        b0 = self._buffer_offset
+        self._key_buffer[:, :, b0:b0 + T] = k
+        self._value_buffer[:, :, b0:b0 + T] = v
+        self._buffer_offset += T
+        if self._buffer_offset > self.buffer_size:
+            self._flush_buffer(B, self._buffer_offset - self.buffer_size)
+
+    def update_and_fetch(self, keys, values):
+        self.append(keys, values)
+        return self.keys, self.values
+
+    # ------------------------------------------------------------ views
+    @property
+    def keys(self) -> torch.Tensor:
+        parts = []
+        if self._compressed_offset > 0:
+            c = self._compressed_offset
+            parts.append(_dequantize_keys(self.codec, self._key_indices[:, :, :c],
+                                          None if self._key_heavy is None else self._key_heavy[:, :, :c]))
+        if self._buffer_offset > 0:
+            parts.append(self._key_buffer[:, :, :self._buffer_offset].float())
+        if not parts:
+            return torch.zeros((max(self._batch, 1), self.n_kv_heads, 0, self.head_dim),
+                               dtype=torch.float32, device=self.device)
+        return torch.cat(parts, dim=2)
+
+    def _compressed_values(self, out_dtype=torch.float16) -> torch.Tensor | None:
+        c = self._compressed_offset
+        if c == 0:
+            return None
+        vc = self._value_codec_impl
+        if self.value_backend == "grouped":
+            return vc.dequantize(self._values_packed[:, :, :c], self._value_scales[:, :, :c],
+                                 self._value_zeros[:, :, :c], out_dtype=out_dtype)
+        if self.value_backend == "turboquant":
+            return vc.dequantize(self._values_packed[:, :, :c], self._value_norms[:, :, :c],
+                                 out_dtype=out_dtype)
+        if self.value_backend == "sunshape":
+            return _dequantize_keys(self.value_codec, self._value_indices[:, :, :c], None).to(out_dtype)
+        return self._values_fp16[:, :, :c]
+
+    @property
+    def values(self) -> torch.Tensor:
+        """Compressed values decoded (in the cache dtype) followed by the buffer."""
+        parts = []
+        cv = self._compressed_values(torch.float16)
+        if cv is not None:
+            parts.append(cv)
+        if self._buffer_offset > 0:
+            parts.append(self._value_buffer[:, :, :self._buffer_offset])
+        if not parts:
+            return torch.zeros((max(self._batch, 1), self.n_kv_heads, 0, self.head_dim),
+                               dtype=self.dtype, device=self.device)
+        return torch.cat(parts, dim=2)
+
+    @property
+    def key_indices(self) -> torch.Tensor:
+        if self._key_indices is None or self._compressed_offset == 0:
+            return torch.zeros((max(self._batch, 1), self.n_kv_heads, 0, self.n_blocks),
+                               dtype=torch.uint8, device=self.device)
+        return self._key_indices[:, :, :self._compressed_offset]
+
+    @property
+    def buffer_keys(self) -> torch.Tensor:
+        if self._key_buffer is None or self._buffer_offset == 0:
+            return torch.zeros((max(self._batch, 1), self.n_kv_heads, 0, self.head_dim),
+                               dtype=torch.float16, device=self.device)
+        return self._key_buffer[:, :, :self._buffer_offset]
+
+    @property
+    def buffer_values(self) -> torch.Tensor:
+        if self._value_buffer is None or self._buffer_offset == 0:
+            return torch.zeros((max(self._batch, 1), self.n_kv_heads, 0, self.head_dim),
+                               dtype=torch.float16, device=self.device)
+        return self._value_buffer[:, :, :self._buffer_offset]
+
+    @property
+    def compressed_offset(self) -> int:
+        return self._compressed_offset
+
+    @property
+    def buffer_offset(self) -> int:
+        return self._buffer_offset
+
+    @property
+    def values_packed_raw(self):
+        if self.value_backend != "grouped" or self._compressed_offset == 0:
+            return None
+        return self._values_packed[:, :, :self._compressed_offset]
+
+    @property
+    def value_scales_raw(self):
+        if self.value_backend != "grouped" or self._compressed_offset == 0:
+            return None
+        return self._value_scales[:, :, :self._compressed_offset]
+
+    @property
+    def value_zeros_raw(self):
+        if self.value_backend != "grouped" or self._compressed_offset == 0:
+            return None
+        return self._value_zeros[:, :, :self._compressed_offset]
+
+    @property
+    def can_fuse_value_dequant(self) -> bool:
+        return self.value_backend == "grouped" and self._compressed_offset > 0
+
+    # ------------------------------------------------------------ fused-attention view
+    def attention_spec(self) -> dict:
+        spec = dict(tc=self._compressed_offset, cap=self._compressed_capacity)
+        if self._compressed_offset > 0:
+            spec["idx"] = self._key_indices
+            if self._key_heavy is not None:
+                spec["kheavy"] = self._key_heavy
+            vc = self._value_codec_impl
+            if self.value_backend == "fp16":
+                spec["v"] = self._values_fp16
+            elif self.value_backend == "sunshape":
+                cap = self._compressed_capacity
+                full = torch.zeros((self._batch, self.n_kv_heads, cap, self.head_dim),
+                                   dtype=torch.float16, device=self.device)
+                full[:, :, :self._compressed_offset] = self._compressed_values(torch.float16)
+                spec["v"] = full
+            elif self.value_backend == "grouped":
+                spec.update(vq=self._values_packed, vs=self._value_scales, vz=self._value_zeros,
+                            bits=vc.bits, group=vc.group_size, levels=vc.levels(self.device))
+            else:
+                norms = self._value_norms
+                spec.update(vq=self._values_packed,
+                            vs=norms if norms.dim() == 4 else norms.unsqueeze(-1), vz=None,
+                            bits=vc.bits, group=vc.group_size or self.head_dim,
+                            levels=vc.levels(self.device), v_rot=vc.rotation)
+        if self._buffer_offset > 0:
+            spec.update(k_tail=self._key_buffer, v_tail=self._value_buffer,
+                        ttail=self._buffer_offset)
+        return spec
+
+    # ------------------------------------------------------------ accounting
+    @property
+    def nbytes(self) -> int:
+        """Storage bytes of compressed + buffered tokens for the real batch size
+        (the reference's version assumes batch 1, cache.py:907)."""
+        B = max(self._batch, 1)
+        H, c, b = self.n_kv_heads, self._compressed_offset, self._buffer_offset
+        idx = B * H * c * self.n_blocks
+        idx += B * H * c * self.codec.n_heavy_blocks * self.block_dim * 2
+        vc = self._value_codec_impl
+        if self.value_backend == "grouped" and c:
+            val = B * H * c * (vc.packed_dim * 4 + vc.n_groups * 8)
+        elif self.value_backend == "turboquant" and c:
+            sc = 4 if vc.group_size is None else 2 * vc.n_scale_groups
+            val = B * H * c * (vc.packed_dim * 4 + sc)
+        elif self.value_backend == "sunshape" and c:
+            val = B * H * c * self.value_n_blocks
+        else:
+            val = B * H * c * self.head_dim * 2
+        return idx + val + B * H * b * self.head_dim * 4
+
+    @property
+    def nbytes_equivalent_fp16(self) -> int:
+        if self.offset == 0:
+            return 0
+        return 2 * max(self._batch, 1) * self.n_kv_heads * self.offset * self.head_dim * 2
+
+    @property
+    def compression_ratio(self) -> float:
+        fp16 = self.nbytes_equivalent_fp16
+        return 1.0 if fp16 == 0 else fp16 / max(1, self.nbytes)
+
+    def is_trimmable(self) -> bool:
+        return True
+
+    def trim(self, n: int) -> None:
+        """Drops n tokens from the end: buffer first, then compressed (cache.py:954-963)."""
+        if n <= 0:
+            return
+        bt = min(n, self._buffer_offset)
+        self._buffer_offset -= bt
+        rest = n - bt
+        if rest > 0:
+            self._compressed_offset = max(0, self._compressed_offset - rest)
+
+    def empty(self) -> bool:
+        return self.offset == 0
+
+    def make_mask(self, N: int, return_array: bool = False, window_size=None, **kwargs):
+        return _causal_mask(self.offset, N, return_array)
+
+    @property
+    def state(self):
+        parts = []
+        if self._compressed_offset > 0:
+            parts.append(self.key_indices)
+        if self._buffer_offset > 0:
+            parts.append(self.buffer_keys)
+        if not parts:
+            parts.append(torch.zeros((1,), device=self.device))
+        return tuple(parts)
+
+    def __repr__(self) -> str:
+        return (f"HybridSunShapeKVCache(offset={self.offset}, compressed={self._compressed_offset}, "
+                f"buffer={self._buffer_offset}, value_backend={self.value_backend}, "
+                f"compression={self.compression_ratio:.1f}x)")
+
+
+def create_kv_cache(codec: SunShapeBlockCodec, *, n_kv_heads: int = 1, head_dim: int | None = None,
+                    dtype=torch.float16, value_backend: str = "fp16", value_bits: int | None = None,
+                    value_group_size: int = 64, value_seed: int = 43,
+                    value_codec: SunShapeBlockCodec | None = None,
+                    buffer_size: int = _DEFAULT_BUFFER_SIZE, prefer_metal_kernels: bool = True,
+                    tq_group_size: int | None = None, value_rotation=None):
+    """cache.py:1006-1107: fp16 values with the default buffer -> simple cache;
+    anything else -> hybrid cache."""
+    if value_backend == "fp16" and buffer_size == _DEFAULT_BUFFER_SIZE:
+        return SunShapeKVCache(codec, n_kv_heads=n_kv_heads, head_dim=head_dim, dtype=dtype)
+    return HybridSunShapeKVCache(
+        codec, n_kv_heads=n_kv_heads, head_dim=head_dim, dtype=dtype, buffer_size=buffer_size,
+        value_backend=value_backend, value_bits=value_bits, value_group_size=value_group_size,
+        value_seed=value_seed, value_codec=value_codec, prefer_metal_kernels=prefer_metal_kernels,
+        tq_group_size=tq_group_size, value_rotation=value_rotation)

@@ -1,0 +1,396 @@
+// Block-VQ codec kernels: nearest-centroid assignment, k-means update,
+// gather scores and reconstruction.
+//
+// Assignment reproduces the reference's CPU arithmetic exactly
+// (codec.py:497-499): d = k - c and d*d are single float32 roundings and the
+// sum over the block follows NumPy's pairwise order (for n < 8 a left-to-right
+// sum; for 8 <= n <= 16 eight partial sums combined as ((0+1)+(2+3))+((4+5)+
+// (6+7))). All float ops use explicit round-to-nearest intrinsics so the
+// compiler cannot contract them into FMAs.
+#include "common.cuh"
+
+namespace ss {
+namespace {
+
+constexpr int kAssignThreads = 512;
+constexpr int kAssignRows = 32;  // rows per tile (one per lane)
+
+// NumPy pairwise sum of n <= 16 float32 terms (numpy/_core/src/umath/loops_utils.h).
+template <int N>
+__device__ __forceinline__ float np_pairwise_sum(const float* r) {
+  if constexpr (N < 8) {
+    float s = r[0];
+#pragma unroll
+    for (int i = 1; i < N; ++i) s = __fadd_rn(s, r[i]);
+    return s;
+  } else {
+    float p[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) p[i] = r[i];
+#pragma unroll
+    for (int i = 8; i + 8 <= N; i += 8) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) p[j] = __fadd_rn(p[j], r[i + j]);
+    }
+    float s = __fadd_rn(__fadd_rn(__fadd_rn(p[0], p[1]), __fadd_rn(p[2], p[3])),
+                        __fadd_rn(__fadd_rn(p[4], p[5]), __fadd_rn(p[6], p[7])));
+#pragma unroll
+    for (int i = (N / 8) * 8; i < N; ++i) s = __fadd_rn(s, r[i]);
+    return s;
+  }
+}
+
+template <int BD>
+__device__ __forceinline__ float dist_direct(const float* kk, const float* c) {
+  float r[BD];
+#pragma unroll
+  for (int j = 0; j < BD; ++j) {
+    float d = __fsub_rn(kk[j], c[j]);
+    r[j] = __fmul_rn(d, d);
+  }
+  return np_pairwise_sum<BD>(r);
+}
+
+struct AssignParams {
+  const void* keys;
+  int key_dtype;
+  int64_t n_groups, rpg, kgs, krs;
+  int d, nb, k;
+  const int32_t* perm;
+  const float* cents;
+  const uint8_t* heavy;
+  uint8_t* out_idx;
+  int64_t igs, irs;
+  uint16_t* out_heavy;
+  int64_t hgs, hrs;
+  float* out_pt;
+  int dist_mode;
+  int b_per_cta;  // blocks handled by one CTA (grid.y = ceil(nb / b_per_cta))
+};
+
+template <int BD>
+__global__ void __launch_bounds__(kAssignThreads) vq_assign_kernel(AssignParams p) {
+  extern __shared__ __align__(16) float sm[];
+  const int b0 = blockIdx.y * p.b_per_cta;
+  const int b1 = min(p.nb, b0 + p.b_per_cta);
+  const int nbl = b1 - b0;
+  float* s_c = sm;                                   // [nbl][k][BD]
+  float* s_csq = s_c + (size_t)nbl * p.k * BD;       // [nbl][k] (expanded mode)
+  float* s_k = s_csq + (size_t)nbl * p.k;            // [32][d + 1]
+  uint8_t* s_idx = reinterpret_cast<uint8_t*>(s_k + kAssignRows * (p.d + 1));  // [32][nb]
+  __shared__ int s_perm[1024];
+  __shared__ uint8_t s_heavy[128];
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int i = tid; i < p.d; i += kAssignThreads) s_perm[i] = p.perm ? p.perm[i] : i;
+  for (int i = tid; i < p.nb; i += kAssignThreads) s_heavy[i] = p.heavy ? p.heavy[i] : 0;
+  const int nc = nbl * p.k * BD;
+  const float* gc = p.cents + (size_t)b0 * p.k * BD;
+  for (int i = tid; i < nc; i += kAssignThreads) s_c[i] = gc[i];
+  __syncthreads();
+  if (p.dist_mode == 1) {
+    for (int i = tid; i < nbl * p.k; i += kAssignThreads) {
+      float r[BD];
+#pragma unroll
+      for (int j = 0; j < BD; ++j) r[j] = __fmul_rn(s_c[i * BD + j], s_c[i * BD + j]);
+      s_csq[i] = np_pairwise_sum<BD>(r);
+    }
+  }
+
+  const int64_t n_rows = p.n_groups * p.rpg;
+  const int64_t n_tiles = (n_rows + kAssignRows - 1) / kAssignRows;
+  for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+    const int64_t r0 = tile * kAssignRows;
+    __syncthreads();  // previous tile's s_k / s_idx fully consumed
+    // Load the permuted key tile as float32.
+    for (int e = tid; e < kAssignRows * p.d; e += kAssignThreads) {
+      const int rr = e / p.d, j = e - rr * p.d;
+      const int64_t r = r0 + rr;
+      float v = 0.f;
+      if (r < n_rows) {
+        const int64_t g = r / p.rpg, t = r - g * p.rpg;
+        const int64_t off = g * p.kgs + t * p.krs + s_perm[j];
+        v = load_as_f32(p.keys, p.key_dtype, off);
+      }
+      s_k[rr * (p.d + 1) + j] = v;
+    }
+    __syncthreads();
+    const int64_t r = r0 + lane;
+    const bool valid = r < n_rows;
+    for (int bl = warp; bl < nbl; bl += kAssignThreads / 32) {
+      const int b = b0 + bl;
+      float kk[BD];
+#pragma unroll
+      for (int j = 0; j < BD; ++j) kk[j] = s_k[lane * (p.d + 1) + b * BD + j];
+      int best_i = 0;
+      if (!s_heavy[b]) {
+        const float* cb = s_c + (size_t)bl * p.k * BD;
+        float best = 0.f;
+        if (p.dist_mode == 0) {
+          best = dist_direct<BD>(kk, cb);
+#pragma unroll 4
+          for (int c = 1; c < p.k; ++c) {
+            const float dd = dist_direct<BD>(kk, cb + c * BD);
+            if (dd < best) { best = dd; best_i = c; }
+          }
+        } else {
+          // ||x||^2 + ||c||^2 - (2x).c, as NumPy/BLAS evaluate codec.py:88-90
+          float r2[BD];
+          float x2[BD];
+#pragma unroll
+          for (int j = 0; j < BD; ++j) {
+            r2[j] = __fmul_rn(kk[j], kk[j]);
+            x2[j] = __fmul_rn(2.0f, kk[j]);
+          }
+          const float xsq = np_pairwise_sum<BD>(r2);
+          const float* csq = s_csq + (size_t)bl * p.k;
+          for (int c = 0; c < p.k; ++c) {
+            float dot = 0.f;
+#pragma unroll
+            for (int j = 0; j < BD; ++j) dot = __fmaf_rn(x2[j], cb[c * BD + j], dot);
+            const float dd = __fsub_rn(__fadd_rn(xsq, csq[c]), dot);
+            if (c == 0 || dd < best) { best = dd; best_i = c; }
+          }
+        }
+      } else if (valid) {
+        const int64_t g = r / p.rpg, t = r - g * p.rpg;
+        if (p.out_heavy) {
+          int hpos = 0;
+          for (int bb = 0; bb < b; ++bb) hpos += s_heavy[bb];
+          uint16_t* dst = p.out_heavy + g * p.hgs + t * p.hrs + hpos * BD;
+#pragma unroll
+          for (int j = 0; j < BD; ++j) dst[j] = f2h(kk[j]);
+        }
+        if (p.out_pt) {
+          float* dst = p.out_pt + r * (int64_t)p.nb * BD + b * BD;
+#pragma unroll
+          for (int j = 0; j < BD; ++j) dst[j] = kk[j];
+        }
+      }
+      s_idx[lane * p.nb + b] = static_cast<uint8_t>(best_i);
+    }
+    __syncthreads();
+    for (int e = tid; e < kAssignRows * nbl; e += kAssignThreads) {
+      const int rr = e / nbl, b = b0 + (e - rr * nbl);
+      const int64_t rw = r0 + rr;
+      if (rw < n_rows) {
+        const int64_t g = rw / p.rpg, t = rw - g * p.rpg;
+        p.out_idx[g * p.igs + t * p.irs + b] = s_idx[rr * p.nb + b];
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ k-means
+// One thread per (block, centroid): scans all rows in order and accumulates
+// the assigned ones with float32 adds (same order as np.add.at).
+__global__ void kmeans_update_kernel(const float* data, int64_t n, int nb, int bd,
+                                     const uint8_t* assign, const float* cin, float* cout,
+                                     int k) {
+  const int gid = blockIdx.x * blockDim.x + threadIdx.x;
+  if (gid >= nb * k) return;
+  const int b = gid / k, c = gid - b * k;
+  float acc[16];
+  for (int j = 0; j < bd; ++j) acc[j] = 0.f;
+  double cnt = 0.0;
+  const int d = nb * bd;
+  for (int64_t i = 0; i < n; ++i) {
+    if (assign[i * nb + b] == c) {
+      const float* x = data + i * d + b * bd;
+      for (int j = 0; j < bd; ++j) acc[j] = __fadd_rn(acc[j], x[j]);
+      cnt += 1.0;
+    }
+  }
+  float* dst = cout + (size_t)gid * bd;
+  const float* src = cin + (size_t)gid * bd;
+  for (int j = 0; j < bd; ++j) {
+    dst[j] = cnt > 0.0 ? static_cast<float>(static_cast<double>(acc[j]) / cnt) : src[j];
+  }
+}
+
+// ------------------------------------------------------------------ scores
+// grid.x over token tiles of 256, grid.y over query chunks of 8; the LUT of
+// the chunk lives in shared memory.
+constexpr int kScoreQ = 8;
+__global__ void __launch_bounds__(256) vq_scores_kernel(const float* q, int nq, int d,
+                                                        const float* cents, int bd, int k,
+                                                        const float* lut_in, int nb,
+                                                        const uint8_t* idx, int64_t t,
+                                                        int64_t irs, float* out, int64_t os) {
+  extern __shared__ float lut[];  // [kScoreQ][nb][k]
+  const int q0 = blockIdx.y * kScoreQ;
+  const int nql = min(kScoreQ, nq - q0);
+  for (int e = threadIdx.x; e < nql * nb * k; e += blockDim.x) {
+    if (lut_in) {
+      lut[e] = lut_in[(size_t)q0 * nb * k + e];
+      continue;
+    }
+    const int qi = e / (nb * k), rem = e - qi * nb * k, b = rem / k, c = rem - b * k;
+    const float* qq = q + (int64_t)(q0 + qi) * d + b * bd;
+    const float* cc = cents + ((size_t)b * k + c) * bd;
+    float acc = 0.f;
+    for (int j = 0; j < bd; ++j) acc = fmaf(qq[j], cc[j], acc);
+    lut[e] = acc;
+  }
+  __syncthreads();
+  const int64_t tok = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (tok >= t) return;
+  const uint8_t* row = idx + tok * irs;
+  for (int qi = 0; qi < nql; ++qi) {
+    const float* l = lut + (size_t)qi * nb * k;
+    float s = 0.f;
+    for (int b = 0; b < nb; ++b) s += l[b * k + row[b]];
+    out[(int64_t)(q0 + qi) * os + tok] = s;
+  }
+}
+
+// ------------------------------------------------------------------ dequant
+__global__ void vq_dequant_kernel(const uint8_t* idx, int64_t n_groups, int64_t rpg,
+                                  int64_t igs, int64_t irs, const float* cents, int d, int bd,
+                                  int k, const int32_t* inv_perm, const uint8_t* heavy,
+                                  const uint16_t* hv, int64_t hgs, int64_t hrs, void* out,
+                                  int odt, int64_t ogs, int64_t ors) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t total = n_groups * rpg * d;
+  if (e >= total) return;
+  const int64_t r = e / d;
+  const int j = static_cast<int>(e - r * d);  // output (original-basis) column
+  const int64_t g = r / rpg, t = r - g * rpg;
+  const int src = inv_perm ? inv_perm[j] : j;  // codec-space column
+  const int b = src / bd, w = src - b * bd;
+  float v;
+  if (heavy && heavy[b]) {
+    int hpos = 0;
+    for (int bb = 0; bb < b; ++bb) hpos += heavy[bb];
+    v = hv ? h2f(hv[g * hgs + t * hrs + hpos * bd + w]) : 0.f;
+  } else {
+    const int c = idx[g * igs + t * irs + b];
+    v = cents[((size_t)b * k + c) * bd + w];
+  }
+  store_from_f32(out, odt, g * ogs + t * ors + j, v);
+}
+
+}  // namespace
+}  // namespace ss
+
+using namespace ss;
+
+extern "C" {
+
+int ss_vq_assign(const void* keys, int key_dtype, int64_t n_groups, int64_t rows_per_group,
+                 int64_t key_group_stride, int64_t key_row_stride, int d, const int32_t* perm,
+                 const float* centroids, int bd, int k, const uint8_t* heavy, uint8_t* out_idx,
+                 int64_t idx_group_stride, int64_t idx_row_stride, uint16_t* out_heavy,
+                 int64_t heavy_group_stride, int64_t heavy_row_stride, float* out_pt,
+                 int dist_mode, void* stream) {
+  SS_REQUIRE(keys && centroids && out_idx, "ss_vq_assign: null pointer");
+  SS_REQUIRE(d > 0 && d <= 1024 && bd > 0 && d % bd == 0, "ss_vq_assign: bad d / bd");
+  SS_REQUIRE(k >= 1 && k <= 256, "ss_vq_assign: k must be in [1, 256] (uint8 indices)");
+  SS_REQUIRE(d / bd <= 128, "ss_vq_assign: at most 128 blocks");
+  SS_REQUIRE(key_dtype >= SS_F32 && key_dtype <= SS_BF16, "ss_vq_assign: bad key dtype");
+  SS_REQUIRE(dist_mode == 0 || dist_mode == 1, "ss_vq_assign: bad dist_mode");
+  count_dispatch("ss_vq_assign");
+  if (n_groups <= 0 || rows_per_group <= 0) return SS_OK;
+  AssignParams p{keys, key_dtype, n_groups, rows_per_group, key_group_stride, key_row_stride,
+                 d, d / bd, k, perm, centroids, heavy, out_idx, idx_group_stride,
+                 idx_row_stride, out_heavy, heavy_group_stride, heavy_row_stride, out_pt,
+                 dist_mode, 0};
+  // Blocks per CTA so that the centroid slice stays within ~160 KB of smem.
+  const size_t per_block = (size_t)k * bd * 4 + (size_t)k * 4;
+  int bpc = static_cast<int>((160 * 1024) / per_block);
+  bpc = bpc < 1 ? 1 : (bpc > p.nb ? p.nb : bpc);
+  p.b_per_cta = bpc;
+  const size_t smem = per_block * bpc + (size_t)kAssignRows * (d + 1) * 4 +
+                      (size_t)kAssignRows * p.nb;
+  const int64_t n_tiles = (n_groups * rows_per_group + kAssignRows - 1) / kAssignRows;
+  const int gy = (p.nb + bpc - 1) / bpc;
+  int gx = sm_count() / gy;
+  if (gx < 1) gx = 1;
+  if (gx > n_tiles) gx = static_cast<int>(n_tiles);
+  dim3 grid(gx, gy);
+  cudaStream_t st = as_stream(stream);
+#define SS_LAUNCH_ASSIGN(BDV)                                                               \
+  case BDV:                                                                                 \
+    cudaFuncSetAttribute(vq_assign_kernel<BDV>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                         (int)smem);                                                       \
+    vq_assign_kernel<BDV><<<grid, kAssignThreads, smem, st>>>(p);                           \
+    break;
+  switch (bd) {
+    SS_LAUNCH_ASSIGN(2)
+    SS_LAUNCH_ASSIGN(4)
+    SS_LAUNCH_ASSIGN(8)
+    SS_LAUNCH_ASSIGN(16)
+    default:
+      return fail(SS_ERR_UNSUPPORTED, "ss_vq_assign: block_dim must be 2, 4, 8 or 16");
+  }
+#undef SS_LAUNCH_ASSIGN
+  return check_launch("ss_vq_assign");
+}
+
+int ss_kmeans_update(const float* data, int64_t n, int nb, int bd, const uint8_t* assign,
+                     const float* cents_in, float* cents_out, int k, void* stream) {
+  SS_REQUIRE(data && assign && cents_in && cents_out, "ss_kmeans_update: null pointer");
+  SS_REQUIRE(cents_in != cents_out, "ss_kmeans_update: cents_in and cents_out alias");
+  SS_REQUIRE(bd >= 1 && bd <= 16 && nb >= 1 && k >= 1 && k <= 256, "ss_kmeans_update: bad dims");
+  count_dispatch("ss_kmeans_update");
+  const int threads = 128;
+  const int blocks = (nb * k + threads - 1) / threads;
+  kmeans_update_kernel<<<blocks, threads, 0, as_stream(stream)>>>(data, n, nb, bd, assign,
+                                                                   cents_in, cents_out, k);
+  return check_launch("ss_kmeans_update");
+}
+
+int ss_vq_scores(const float* q, int nq, int d, const float* centroids, int bd, int k,
+                 const uint8_t* idx, int64_t t, int64_t idx_row_stride, float* out,
+                 int64_t out_stride, void* stream) {
+  SS_REQUIRE(q && centroids && out && (idx || t == 0), "ss_vq_scores: null pointer");
+  SS_REQUIRE(bd > 0 && d % bd == 0 && k >= 1 && k <= 256, "ss_vq_scores: bad dims");
+  const size_t smem = (size_t)kScoreQ * (d / bd) * k * 4;
+  SS_REQUIRE(smem <= 200 * 1024, "ss_vq_scores: lookup table too large for shared memory");
+  count_dispatch("ss_vq_scores");
+  if (nq <= 0 || t <= 0) return SS_OK;
+  cudaFuncSetAttribute(vq_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  dim3 grid(static_cast<unsigned>((t + 255) / 256), (nq + kScoreQ - 1) / kScoreQ);
+  vq_scores_kernel<<<grid, 256, smem, as_stream(stream)>>>(q, nq, d, centroids, bd, k, nullptr,
+                                                           d / bd, idx, t, idx_row_stride, out,
+                                                           out_stride);
+  return check_launch("ss_vq_scores");
+}
+
+int ss_vq_scores_lut(const float* qdots, int nq, int nb, int k, const uint8_t* idx, int64_t t,
+                     int64_t idx_row_stride, float* out, int64_t out_stride, void* stream) {
+  SS_REQUIRE(qdots && out && (idx || t == 0), "ss_vq_scores_lut: null pointer");
+  SS_REQUIRE(nb >= 1 && k >= 1 && k <= 256, "ss_vq_scores_lut: bad dims");
+  const size_t smem = (size_t)kScoreQ * nb * k * 4;
+  SS_REQUIRE(smem <= 200 * 1024, "ss_vq_scores_lut: lookup table too large for shared memory");
+  count_dispatch("ss_vq_scores_lut");
+  if (nq <= 0 || t <= 0) return SS_OK;
+  cudaFuncSetAttribute(vq_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  dim3 grid(static_cast<unsigned>((t + 255) / 256), (nq + kScoreQ - 1) / kScoreQ);
+  vq_scores_kernel<<<grid, 256, smem, as_stream(stream)>>>(nullptr, nq, 0, nullptr, 1, k, qdots,
+                                                           nb, idx, t, idx_row_stride, out,
+                                                           out_stride);
+  return check_launch("ss_vq_scores_lut");
+}
+
+int ss_vq_dequant(const uint8_t* idx, int64_t n_groups, int64_t rows_per_group,
+                  int64_t idx_group_stride, int64_t idx_row_stride, const float* centroids,
+                  int d, int bd, int k, const int32_t* inv_perm, const uint8_t* heavy,
+                  const uint16_t* heavy_vals, int64_t heavy_group_stride,
+                  int64_t heavy_row_stride, void* out, int out_dtype, int64_t out_group_stride,
+                  int64_t out_row_stride, void* stream) {
+  SS_REQUIRE(idx && centroids && out, "ss_vq_dequant: null pointer");
+  SS_REQUIRE(bd > 0 && d % bd == 0 && k >= 1 && k <= 256, "ss_vq_dequant: bad dims");
+  count_dispatch("ss_vq_dequant");
+  const int64_t total = n_groups * rows_per_group * d;
+  if (total <= 0) return SS_OK;
+  const int threads = 256;
+  vq_dequant_kernel<<<static_cast<unsigned>((total + threads - 1) / threads), threads, 0,
+                      as_stream(stream)>>>(
+      idx, n_groups, rows_per_group, idx_group_stride, idx_row_stride, centroids, d, bd, k,
+      inv_perm, heavy, heavy_vals, heavy_group_stride, heavy_row_stride, out, out_dtype,
+      out_group_stride, out_row_stride);
+  return check_launch("ss_vq_dequant");
+}
+
+}  // extern "C"
