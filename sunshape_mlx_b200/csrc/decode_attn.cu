@@ -666,7 +666,7 @@ struct Plan {
   size_t ws_bytes, off_counters, off_slots;
 };
 
-constexpr size_t kSmemBudget = 227 * 1024;
+constexpr size_t kSmemBudget = 226 * 1024;  // leaves room for static barriers
 
 int make_plan(const ss_decode_args* a, Plan& pl) {
   SS_REQUIRE(a, "ss_decode_attn: null args");
@@ -782,8 +782,27 @@ int run_decode(const ss_decode_args* a, float* part_out, void* stream) {
   const int nb = a->d / a->bd;
   const int64_t rows_cap = a->v_pair_stride / a->d;
   // 16-byte alignment of every bulk-copied row block
-  SS_REQUIRE((a->idx_pair_stride * 1) % 16 == 0, "ss_decode_attn: idx pair stride must be 16B");
-  SS_REQUIRE(reinterpret_cast<uintptr_t>(a->idx) % 16 == 0, "ss_decode_attn: idx not 16B aligned");
+  auto aligned = [](const void* ptr, int64_t pair_stride_bytes) {
+    return reinterpret_cast<uintptr_t>(ptr) % 16 == 0 && pair_stride_bytes % 16 == 0;
+  };
+  if (a->tc > 0) {
+    SS_REQUIRE(aligned(a->idx, a->idx_pair_stride),
+               "ss_decode_attn: idx base / pair stride must be 16-byte aligned");
+    if (a->vfmt == SS_V_QUANT) {
+      const int sb = a->v_scale_dtype == SS_F32 ? 4 : 2;
+      SS_REQUIRE(aligned(a->vq, a->vq_pair_stride * 4) &&
+                     aligned(a->v_scales, a->vs_pair_stride * sb) &&
+                     (!a->v_zeros || aligned(a->v_zeros, a->vz_pair_stride * 4)),
+                 "ss_decode_attn: quantized value streams must be 16-byte aligned");
+    }
+    if (a->n_heavy)
+      SS_REQUIRE(aligned(a->kheavy, a->kheavy_pair_stride * 2),
+                 "ss_decode_attn: heavy key stream must be 16-byte aligned");
+  }
+  if (a->ttail > 0)
+    SS_REQUIRE(aligned(a->k_tail, a->tail_pair_stride * 2) &&
+                   aligned(a->v_tail, a->tail_pair_stride * 2),
+               "ss_decode_attn: tail streams must be 16-byte aligned");
   CUtensorMap mv{}, mvt{};
   if (a->vfmt == SS_V_F16 && a->tc > 0) {
     SS_REQUIRE(a->v_pair_stride % a->d == 0 && rows_cap >= a->tc, "ss_decode_attn: bad v stride");
