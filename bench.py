@@ -344,6 +344,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="build the workload, run warmup+steps decode launches, exit "
+                         "(short command for ncu captures)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -358,6 +361,18 @@ def main():
     if world > 1:
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    if args.profile:
+        from sunshape_mlx_b200.attention import PreparedDecode
+
+        dev = torch.device("cuda", local)
+        torch.cuda.set_device(dev)
+        _, cache, q = build_workload(rank, dev)
+        prep = PreparedDecode(q, cache, 1 / math.sqrt(D))
+        for _ in range(args.warmup + args.steps):
+            prep.run()
+        torch.cuda.synchronize()
+        print("profile run done", flush=True)
+        return
     try:
         line = run_ours(args, world, rank, local)
         if line is not None:

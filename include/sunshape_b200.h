@@ -222,7 +222,8 @@ typedef struct ss_decode_args {
   const float* v_zeros; int64_t vz_pair_stride;        /* rows d/v_group or NULL */
   float v_levels[16];        /* level table for SS_V_QUANT */
   const float* v_rot;        /* f32 (d,d): value = r @ R, or NULL */
-  /* fp16 tail (hybrid buffer), original basis */
+  /* fp16 tail (hybrid buffer): keys in the original basis; values in the
+   * original basis, or already rotated (v R^T) when v_rot is set */
   int64_t ttail;
   const uint16_t* k_tail; const uint16_t* v_tail; int64_t tail_pair_stride;
   /* masking */

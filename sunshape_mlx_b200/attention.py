@@ -93,13 +93,13 @@ def _fill_args(q: torch.Tensor, centroids: torch.Tensor, perm, scale: float, spe
                 a.vz_pair_stride = vz.stride(1)
             lv = list(spec["levels"]) + [0.0] * (16 - len(spec["levels"]))
             a.v_levels = (C.c_float * 16)(*lv)
-            vr = spec.get("v_rot")
-            if vr is not None:
-                vr = vr.contiguous()
-                keep.append(vr)
-                a.v_rot = vr.data_ptr()
     else:
         a.vfmt = L.SS_V_F16 if v is not None or vq is None else L.SS_V_QUANT
+    vr = spec.get("v_rot")
+    if vr is not None:
+        vr = vr.contiguous()
+        keep.append(vr)
+        a.v_rot = vr.data_ptr()
     tt = int(spec.get("ttail", 0))
     a.ttail = tt
     if tt > 0:

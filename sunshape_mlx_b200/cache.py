@@ -284,6 +284,9 @@ class HybridSunShapeKVCache:
         self._batch = 0
         self._key_buffer = None
         self._value_buffer = None
+        # TurboQuant values are attended in the rotated basis; the fp16 tail is
+        # kept there too (v R^T) so one accumulator covers all tokens.
+        self._value_buffer_rot = None
         self._key_indices = None
         self._key_heavy = None
         self._values_packed = None
@@ -359,6 +362,8 @@ class HybridSunShapeKVCache:
         if rem > 0:
             self._key_buffer[:, :, :rem] = self._key_buffer[:, :, n:n + rem].clone()
             self._value_buffer[:, :, :rem] = self._value_buffer[:, :, n:n + rem].clone()
+            if self._value_buffer_rot is not None:
+                self._value_buffer_rot[:, :, :rem] = self._value_buffer_rot[:, :, n:n + rem].clone()
         self._compressed_offset += n
         self._buffer_offset = rem
 
@@ -380,9 +385,16 @@ class HybridSunShapeKVCache:
                                      torch.float16, self.device)
             self._value_buffer = _grow(self._value_buffer, (B, H, size, D), self._buffer_offset,
                                        torch.float16, self.device)
+            if self.value_backend == "turboquant":
+                self._value_buffer_rot = _grow(self._value_buffer_rot, (B, H, size, D),
+                                               self._buffer_offset, torch.float16, self.device)
         b0 = self._buffer_offset
         self._key_buffer[:, :, b0:b0 + T] = k
         self._value_buffer[:, :, b0:b0 + T] = v
+        if self._value_buffer_rot is not None:
+            from .rotation import _matmul_f32
+            rt = self._value_codec_impl.rotation_t
+            self._value_buffer_rot[:, :, b0:b0 + T] = _matmul_f32(v.float(), rt).half()
         self._buffer_offset += T
         if self._buffer_offset > self.buffer_size:
             self._flush_buffer(B, self._buffer_offset - self.buffer_size)
@@ -512,8 +524,10 @@ class HybridSunShapeKVCache:
                             bits=vc.bits, group=vc.group_size or self.head_dim,
                             levels=vc.levels(self.device), v_rot=vc.rotation)
         if self._buffer_offset > 0:
-            spec.update(k_tail=self._key_buffer, v_tail=self._value_buffer,
-                        ttail=self._buffer_offset)
+            vt = self._value_buffer_rot if self._value_buffer_rot is not None else self._value_buffer
+            spec.update(k_tail=self._key_buffer, v_tail=vt, ttail=self._buffer_offset)
+            if self._value_buffer_rot is not None and "v_rot" not in spec:
+                spec["v_rot"] = self._value_codec_impl.rotation
         return spec
 
     # ------------------------------------------------------------ accounting

@@ -112,8 +112,6 @@ struct Misc {  // small shared-memory state
   float qo[8][128];     // scaled queries, original basis
   float qc[8][128];     // scaled queries, codec space
   float o[8][128];      // finalisation staging
-  float wmax[kConsumerWarps][8];
-  float wsum[kConsumerWarps][8];
   float mrow[8], lrow[8];
   float levels[16];
   int heavy_pos[32];
@@ -134,10 +132,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int TILE = p.tile;
-  const int TPT = kConsumers / TILE;  // threads per token in the score phase
+  const int wpt = TILE / 16;                   // warps sharing one tile (16 tokens each)
   Misc& ms = *reinterpret_cast<Misc*>(smem + p.off_misc);
   float* lut = reinterpret_cast<float*>(smem + p.off_lut);
-  __half* P = reinterpret_cast<__half*>(smem + p.off_p);  // [TILE][8]
 
   const int64_t cta = blockIdx.x;
   const int64_t t_begin = range_start(cta, p.total_tiles, p.grid);
@@ -146,7 +143,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
   if (tid == 0) {
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], kConsumerWarps);
+      mbar_init(&empty_bar[s], wpt);
     }
     ms.abort = 0;
     int hp = 0;
@@ -179,7 +176,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
         const int64_t u = tau / p.tpu;
         const int lt = static_cast<int>(tau - u * p.tpu);
         const int64_t pair = u / p.n_rg;
-        uint8_t* st = smem + p.off_stage + (size_t)s * p.stage_bytes;
+        uint8_t* st = smem + (size_t)s * p.stage_bytes;
         if (lt < p.n_ct) {
           const int64_t t0 = (int64_t)lt * TILE;
           uint32_t bytes = TILE * p.nb;
@@ -244,37 +241,41 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
   }
 
   // ====================================================== consumer warps
-  const int ctid = tid;  // 0..255
-  const int tok = ctid / TPT, part = ctid % TPT;
-  const int nbp = p.nb / TPT;  // blocks per thread in the score phase
+  // Warp w owns 16-token slice (w % wpt) of every tile of tile group (w / wpt);
+  // two lanes per token, each summing half of the blocks.
+  constexpr int MT = D / 16;                   // 16-dim MMA tiles of the output
+  const int tgroups = kConsumerWarps / wpt;
+  const int wgroup = warp / wpt, slice = warp % wpt;
+  const int ltok = lane >> 1, part = lane & 1;
+  const int tok = slice * 16 + ltok;           // token within the tile
+  const int nbp = p.nb / 2;
+  const int ctid = tid;                        // 0..255
   const int64_t q_off = p.tc + p.ttail - p.tq;
-  const int mw = warp;  // this warp's 16-dim slice of the output in the MMA phase
-  const bool mma_warp = (mw * 16) < D;
+  __half* Pw = reinterpret_cast<__half*>(smem + p.off_p) + warp * 16 * 8;  // [16][8]
+  uint8_t* vdq_w = smem + p.off_vdq + warp * (16 * D * 2);
+  const uint32_t pw_addr = smem_u32(Pw) + (lane & 15) * 16;
+  const int mi = lane >> 3, mj = lane & 7;
+  const int kk_off = (mi >= 2 ? 8 : 0) + mj;   // ldmatrix row (token) of this lane
+  const int dim_off = (mi & 1) ? 8 : 0;
+  const int rows_valid = p.nrep * p.tq;
 
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  float m_run[R], l_run[R];
-  int it = 0;
-  int64_t cur_unit = -1;
-
-  for (int64_t tau = t_begin; tau < t_end; ++tau, ++it) {
+  int64_t tau = t_begin;
+  while (tau < t_end) {
     const int64_t u = tau / p.tpu;
-    const int lt = static_cast<int>(tau - u * p.tpu);
+    const int64_t u_end = min(t_end, (u + 1) * p.tpu);
     const int64_t pair = u / p.n_rg;
     const int rg = static_cast<int>(u - pair * p.n_rg);
     const int bb = static_cast<int>(pair / p.hkv), hh = static_cast<int>(pair % p.hkv);
 
-    // ---------------------------------------------- new unit: build the LUT
-    if (u != cur_unit) {
-      cur_unit = u;
-      for (int r = 0; r < R; ++r) { m_run[r] = -INFINITY; l_run[r] = 0.f; }
-      acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
-      named_bar_sync(1, kConsumers);  // previous unit fully finalised
+    // ---------------------------------------------- build the unit's LUT
+    named_bar_sync(1, kConsumers);  // previous unit finalised, LUT region free
+    {
       const float sc = round_to(p.scale, p.qdt);
       for (int e = ctid; e < R * p.d; e += kConsumers) {
         const int r = e / p.d, j = e - r * p.d;
         const int rr = rg * R + r;
         float v = 0.f;
-        if (rr < p.nrep * p.tq) {
+        if (rr < rows_valid) {
           const int rep = rr / p.tq, tqi = rr - rep * p.tq;
           const int qh = hh * p.nrep + rep;
           const float x = load_as_f32(p.q, p.qdt, bb * p.q_sb + qh * p.q_sh + tqi * p.q_st + j);
@@ -315,233 +316,267 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
       named_bar_sync(1, kConsumers);
     }
 
-    // ---------------------------------------------- wait for the stage
-    const int s = it % p.stages;
-    if (!ms.abort && !mbar_wait_bounded(&full_bar[s], (it / p.stages) & 1, kWaitLimitNs)) {
-      ms.abort = 1;
-      atomicOr(p.err, 4);
-    }
-    const bool aborted = ms.abort != 0;
-    uint8_t* st = smem + p.off_stage + (size_t)s * p.stage_bytes;
-    const bool compressed = lt < p.n_ct;
-    const int64_t t0 = compressed ? (int64_t)lt * TILE : (int64_t)(lt - p.n_ct) * TILE;
-    const int64_t len = compressed ? p.tc : p.ttail;
-    const int64_t t = t0 + tok;
-    const bool tvalid = t < len && !aborted;
-    const int64_t tg = compressed ? t : p.tc + t;  // position in the whole sequence
+    // ---------------------------------------------- this warp's slices of the unit
+    float m_w[R], l_l[R];
+    float acc[MT][4];
+#pragma unroll
+    for (int r = 0; r < R; ++r) { m_w[r] = -INFINITY; l_l[r] = 0.f; }
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
 
-    // ---------------------------------------------- 1. scores
-    float sc[R];
+    for (int64_t t2 = tau; t2 < u_end; ++t2) {
+      const int it = static_cast<int>(t2 - t_begin);
+      if (it % tgroups != wgroup) continue;
+      const int lt = static_cast<int>(t2 - u * p.tpu);
+      const int s = it % p.stages;
+      if (!ms.abort && !mbar_wait_bounded(&full_bar[s], (it / p.stages) & 1, kWaitLimitNs)) {
+        ms.abort = 1;
+        atomicOr(p.err, 4);
+      }
+      const bool aborted = ms.abort != 0;
+      uint8_t* st = smem + (size_t)s * p.stage_bytes;
+      const bool compressed = lt < p.n_ct;
+      const int64_t t0 = compressed ? (int64_t)lt * TILE : (int64_t)(lt - p.n_ct) * TILE;
+      const int64_t len = compressed ? p.tc : p.ttail;
+      const int64_t t = t0 + tok;
+      const bool tvalid = t < len && !aborted;
+      const int64_t tg = compressed ? t : p.tc + t;
+
+      // 1. scores of this lane's token (half of the blocks)
+      float sc[R];
 #pragma unroll
-    for (int r = 0; r < R; ++r) sc[r] = 0.f;
-    if (tvalid) {
-      if (compressed) {
-        const uint8_t* irow = st + p.off_idx + tok * p.nb + part * nbp;
-        for (int j = 0; j < nbp; ++j) {
-          const int b = part * nbp + j;
-          const float* e = lut + ((size_t)b * p.k + irow[j]) * R;
-          if constexpr (R == 4) {
-            const float4 v = *reinterpret_cast<const float4*>(e);
-            sc[0] += v.x; sc[1] += v.y; sc[2] += v.z; sc[3] += v.w;
-          } else if constexpr (R == 8) {
-            const float4 v0 = *reinterpret_cast<const float4*>(e);
-            const float4 v1 = *reinterpret_cast<const float4*>(e + 4);
-            sc[0] += v0.x; sc[1] += v0.y; sc[2] += v0.z; sc[3] += v0.w;
-            sc[4] += v1.x; sc[5] += v1.y; sc[6] += v1.z; sc[7] += v1.w;
-          } else {
+      for (int r = 0; r < R; ++r) sc[r] = 0.f;
+      if (tvalid) {
+        if (compressed) {
+          const uint8_t* irow = st + p.off_idx + tok * p.nb + part * nbp;
+          for (int j0 = 0; j0 < nbp; j0 += 8) {
+            const uint2 raw = *reinterpret_cast<const uint2*>(irow + j0);
+            const uint32_t w2[2] = {raw.x, raw.y};
 #pragma unroll
-            for (int r = 0; r < R; ++r) sc[r] += e[r];
+            for (int j = 0; j < 8; ++j) {
+              if (j0 + j >= nbp) break;
+              const int b = part * nbp + j0 + j;
+              const uint32_t c = (w2[j >> 2] >> ((j & 3) * 8)) & 0xffu;
+              const float* e = lut + ((size_t)b * p.k + c) * R;
+              if constexpr (R == 4) {
+                const float4 v = *reinterpret_cast<const float4*>(e);
+                sc[0] += v.x; sc[1] += v.y; sc[2] += v.z; sc[3] += v.w;
+              } else if constexpr (R == 8) {
+                const float4 v0 = *reinterpret_cast<const float4*>(e);
+                const float4 v1 = *reinterpret_cast<const float4*>(e + 4);
+                sc[0] += v0.x; sc[1] += v0.y; sc[2] += v0.z; sc[3] += v0.w;
+                sc[4] += v1.x; sc[5] += v1.y; sc[6] += v1.z; sc[7] += v1.w;
+              } else {
+#pragma unroll
+                for (int r = 0; r < R; ++r) sc[r] += e[r];
+              }
+            }
           }
-        }
-        if (p.n_heavy) {
-          int off = p.off_aux;
-          if (p.vfmt != SS_V_F16) {
-            off += TILE * p.v_words * 4 + TILE * p.v_groups * (p.vs_dt == SS_F32 ? 4 : 2);
-            if (p.vz) off += TILE * p.v_groups * 4;
-          }
-          const uint16_t* hrow =
-              reinterpret_cast<const uint16_t*>(st + off) + (size_t)tok * p.n_heavy * p.bd;
-          for (int hj = part; hj < p.n_heavy; hj += TPT) {
-            const int b = ms.heavy_pos[hj];
-            for (int j = 0; j < p.bd; ++j) {
-              const float kv = h2f(hrow[hj * p.bd + j]);
+          if (p.n_heavy) {
+            int off = p.off_aux;
+            if (p.vfmt != SS_V_F16) {
+              off += TILE * p.v_words * 4 + TILE * p.v_groups * (p.vs_dt == SS_F32 ? 4 : 2);
+              if (p.vz) off += TILE * p.v_groups * 4;
+            }
+            const uint16_t* hrow =
+                reinterpret_cast<const uint16_t*>(st + off) + (size_t)tok * p.n_heavy * p.bd;
+            for (int hj = part; hj < p.n_heavy; hj += 2) {
+              const int b = ms.heavy_pos[hj];
+              for (int j = 0; j < p.bd; ++j) {
+                const float kv = h2f(hrow[hj * p.bd + j]);
 #pragma unroll
-              for (int r = 0; r < R; ++r) sc[r] = fmaf(ms.qc[r][b * p.bd + j], kv, sc[r]);
+                for (int r = 0; r < R; ++r) sc[r] = fmaf(ms.qc[r][b * p.bd + j], kv, sc[r]);
+              }
+            }
+          }
+        } else {
+          const uint16_t* krow = p.k_tail + pair * p.tail_ps + t * D;
+          constexpr int per = D / 2;
+          for (int j0 = part * per; j0 < (part + 1) * per; j0 += 8) {
+            const uint4 raw = *reinterpret_cast<const uint4*>(krow + j0);
+            const uint16_t* hv = reinterpret_cast<const uint16_t*>(&raw);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float kv = h2f(hv[j]);
+#pragma unroll
+              for (int r = 0; r < R; ++r) sc[r] = fmaf(ms.qo[r][j0 + j], kv, sc[r]);
             }
           }
         }
-      } else {
-        const uint16_t* krow = p.k_tail + pair * p.tail_ps + t * D;
-        const int per = D / TPT;
-        for (int j0 = part * per; j0 < (part + 1) * per; j0 += 8) {
-          const uint4 raw = *reinterpret_cast<const uint4*>(krow + j0);
-          const uint16_t* hv = reinterpret_cast<const uint16_t*>(&raw);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float kv = h2f(hv[j]);
-#pragma unroll
-            for (int r = 0; r < R; ++r) sc[r] = fmaf(ms.qo[r][j0 + j], kv, sc[r]);
-          }
-        }
       }
-    }
-    // reduce the TPT partial sums of a token
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      for (int o = 1; o < TPT; o <<= 1) sc[r] += __shfl_xor_sync(0xffffffffu, sc[r], o);
-    }
-    // masking
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int rr = rg * R + r;
-      bool ok = tvalid && rr < p.nrep * p.tq;
-      const int tqi = rr % p.tq;
-      if (ok && p.causal && tg > q_off + tqi) ok = false;
-      if (ok && p.mask) {
-        const float mv = p.mask[tqi * p.mask_stride + tg];
-        if (p.mask_mode == 0) sc[r] += mv;
-        else if (mv == 0.f) sc[r] = -FLT_MAX;
-      }
-      if (!ok) sc[r] = -INFINITY;
-    }
-
-    // ---------------------------------------------- 2. online softmax
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      float mx = sc[r];
-      for (int o = TPT; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      if (lane == 0) ms.wmax[warp][r] = mx;
-    }
-    named_bar_sync(1, kConsumers);
-    float m_new[R], alpha[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      float mx = m_run[r];
-      for (int w = 0; w < kConsumerWarps; ++w) mx = fmaxf(mx, ms.wmax[w][r]);
-      m_new[r] = mx;
-      alpha[r] = (mx == -INFINITY) ? 1.f : exp2f((m_run[r] - mx) * kLog2e);
-    }
-    float pv[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      float e = 0.f;
-      if (sc[r] != -INFINITY) e = exp2f((sc[r] - m_new[r]) * kLog2e);
-      const __half h = __float2half_rn(e);
-      pv[r] = __half2float(h);
-      if (part == 0) P[tok * 8 + r] = h;
-    }
-    if (part == 0) {
-      for (int r = R; r < 8; ++r) P[tok * 8 + r] = __float2half_rn(0.f);
-    }
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      float sm = part == 0 ? pv[r] : 0.f;
-      for (int o = 1; o < 32; o <<= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
-      if (lane == 0) ms.wsum[warp][r] = sm;
-    }
-
-    // quantized values / tail values of the quantized path -> fp16 tile
-    uint32_t vbase = smem_u32(st);
-    if (p.vfmt != SS_V_F16) {
-      uint8_t* vdq = smem + p.off_vdq;
-      vbase = smem_u32(vdq);
-      if (compressed) {
-        const uint32_t* words = reinterpret_cast<const uint32_t*>(st + p.off_aux);
-        const uint8_t* sp = st + p.off_aux + TILE * p.v_words * 4;
-        const float* zp = p.vz ? reinterpret_cast<const float*>(
-                                     sp + TILE * p.v_groups * (p.vs_dt == SS_F32 ? 4 : 2))
-                               : nullptr;
-        const int vpw = p.v_bits == 3 ? 10 : 32 / p.v_bits;
-        const uint32_t msk = (1u << p.v_bits) - 1u;
-        // one 16-byte chunk (8 channels of one token) per step
-        for (int e = ctid; e < TILE * (D / 8); e += kConsumers) {
-          const int tk = e / (D / 8), ch = e - tk * (D / 8);
-          float vals[8];
-          const int gi = (ch * 8) / p.v_group;
-          const float s_ = p.vs_dt == SS_F32
-                               ? reinterpret_cast<const float*>(sp)[tk * p.v_groups + gi]
-                               : h2f(reinterpret_cast<const uint16_t*>(sp)[tk * p.v_groups + gi]);
-          const float z_ = zp ? zp[tk * p.v_groups + gi] : 0.f;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const int c = ch * 8 + j;
-            const uint32_t code = (words[tk * p.v_words + c / vpw] >> ((c % vpw) * p.v_bits)) & msk;
-            float x = __fmul_rn(ms.levels[code], s_);
-            if (zp) x = __fadd_rn(x, z_);
-            vals[j] = x;
-          }
-          uint4 pk;
-          pk.x = pack_h2(vals[0], vals[1]);
-          pk.y = pack_h2(vals[2], vals[3]);
-          pk.z = pack_h2(vals[4], vals[5]);
-          pk.w = pack_h2(vals[6], vals[7]);
-          const uint32_t a = vtile_addr(0, TILE, tk, ch * 8);
-          *reinterpret_cast<uint4*>(vdq + a) = pk;
-        }
-      } else {
-        for (int e = ctid; e < TILE * (D / 8); e += kConsumers) {
-          const int tk = e / (D / 8), ch = e - tk * (D / 8);
-          uint4 pk = make_uint4(0, 0, 0, 0);
-          if (t0 + tk < len)
-            pk = *reinterpret_cast<const uint4*>(p.v_tail + pair * p.tail_ps + (t0 + tk) * D +
-                                                 ch * 8);
-          *reinterpret_cast<uint4*>(vdq + vtile_addr(0, TILE, tk, ch * 8)) = pk;
-        }
-      }
-    }
-    named_bar_sync(1, kConsumers);
-
-    // ---------------------------------------------- 3. P.V on tensor cores
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      float sum = 0.f;
-      for (int w = 0; w < kConsumerWarps; ++w) sum += ms.wsum[w][r];
-      l_run[r] = l_run[r] * alpha[r] + sum;
-      m_run[r] = m_new[r];
-    }
-    if (mma_warp) {
-      const int n0 = 2 * (lane & 3);
-      float a0 = 1.f, a1 = 1.f;
+      for (int r = 0; r < R; ++r) sc[r] += __shfl_xor_sync(0xffffffffu, sc[r], 1);
 #pragma unroll
       for (int r = 0; r < R; ++r) {
-        if (r == n0) a0 = alpha[r];
-        if (r == n0 + 1) a1 = alpha[r];
+        const int rr = rg * R + r;
+        bool ok = tvalid && rr < rows_valid;
+        const int tqi = rr % p.tq;
+        if (ok && p.causal && tg > q_off + tqi) ok = false;
+        if (ok && p.mask) {
+          const float mv = p.mask[tqi * p.mask_stride + tg];
+          if (p.mask_mode == 0) sc[r] += mv;
+          else if (mv == 0.f) sc[r] = -FLT_MAX;
+        }
+        if (!ok) sc[r] = -INFINITY;
       }
-      acc[0] *= a0; acc[1] *= a1; acc[2] *= a0; acc[3] *= a1;
-      const int mi = lane >> 3, mj = lane & 7;
-      const int kk_off = (mi >= 2 ? 8 : 0) + mj;
-      const int dim = mw * 16 + ((mi & 1) ? 8 : 0);
-      const uint32_t pbase = smem_u32(P);
-      for (int ks = 0; ks < TILE; ks += 16) {
-        uint32_t x0, x1, x2, x3, y0, y1;
-        ldsm_x4_trans(vtile_addr(vbase, TILE, ks + kk_off, dim), x0, x1, x2, x3);
-        ldsm_x2_trans(pbase + (ks + (lane & 15)) * 16, y0, y1);
-        mma_16816(acc, x0, x1, x2, x3, y0, y1);
+
+      // 2. online softmax over this warp's slice
+      float alpha[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        float mx = sc[r];
+#pragma unroll
+        for (int o = 2; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const float mn = fmaxf(m_w[r], mx);
+        alpha[r] = (mn == -INFINITY) ? 1.f : exp2f((m_w[r] - mn) * kLog2e);
+        const float e = (sc[r] == -INFINITY) ? 0.f : exp2f((sc[r] - mn) * kLog2e);
+        const __half h = __float2half_rn(e);
+        if (part == 0) {
+          Pw[ltok * 8 + r] = h;
+          l_l[r] = l_l[r] * alpha[r] + __half2float(h);
+        } else {
+          l_l[r] *= alpha[r];
+        }
+        m_w[r] = mn;
+      }
+      if (part == 0) {
+#pragma unroll
+        for (int r = R; r < 8; ++r) Pw[ltok * 8 + r] = __float2half_rn(0.f);
+      }
+
+      // quantized values (or the quantized path's tail) -> this warp's fp16 slice
+      uint32_t vbase;
+      int vrows, vtok;
+      if (p.vfmt == SS_V_F16) {
+        vbase = smem_u32(st);
+        vrows = TILE;
+        vtok = slice * 16;
+      } else {
+        vbase = smem_u32(vdq_w);
+        vrows = 16;
+        vtok = 0;
+        if (compressed) {
+          const uint32_t* words = reinterpret_cast<const uint32_t*>(st + p.off_aux);
+          const uint8_t* sp = st + p.off_aux + TILE * p.v_words * 4;
+          const float* zp = p.vz ? reinterpret_cast<const float*>(
+                                       sp + TILE * p.v_groups * (p.vs_dt == SS_F32 ? 4 : 2))
+                                 : nullptr;
+          const int vpw = p.v_bits == 3 ? 10 : 32 / p.v_bits;
+          const uint32_t msk = (1u << p.v_bits) - 1u;
+          for (int e = lane; e < 16 * (D / 8); e += 32) {
+            const int tk = e / (D / 8), ch = e - tk * (D / 8);
+            const int tt = slice * 16 + tk;
+            const int gi = (ch * 8) / p.v_group;
+            const float s_ = p.vs_dt == SS_F32
+                                 ? reinterpret_cast<const float*>(sp)[tt * p.v_groups + gi]
+                                 : h2f(reinterpret_cast<const uint16_t*>(sp)[tt * p.v_groups + gi]);
+            const float z_ = zp ? zp[tt * p.v_groups + gi] : 0.f;
+            float vals[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int c = ch * 8 + j;
+              const uint32_t code = (words[tt * p.v_words + c / vpw] >> ((c % vpw) * p.v_bits)) & msk;
+              float x = __fmul_rn(ms.levels[code], s_);
+              if (zp) x = __fadd_rn(x, z_);
+              vals[j] = x;
+            }
+            uint4 pk;
+            pk.x = pack_h2(vals[0], vals[1]);
+            pk.y = pack_h2(vals[2], vals[3]);
+            pk.z = pack_h2(vals[4], vals[5]);
+            pk.w = pack_h2(vals[6], vals[7]);
+            *reinterpret_cast<uint4*>(vdq_w + vtile_addr(0, 16, tk, ch * 8)) = pk;
+          }
+        } else {
+          for (int e = lane; e < 16 * (D / 8); e += 32) {
+            const int tk = e / (D / 8), ch = e - tk * (D / 8);
+            const int64_t tt = t0 + slice * 16 + tk;
+            uint4 pk = make_uint4(0, 0, 0, 0);
+            if (tt < len)
+              pk = *reinterpret_cast<const uint4*>(p.v_tail + pair * p.tail_ps + tt * D + ch * 8);
+            *reinterpret_cast<uint4*>(vdq_w + vtile_addr(0, 16, tk, ch * 8)) = pk;
+          }
+        }
+      }
+      __syncwarp();
+
+      // 3. P.V: O^T[dims][rows] += V^T[dims][16 tokens] . P[16 tokens][rows]
+      {
+        const int n0 = 2 * (lane & 3);
+        float a0 = 1.f, a1 = 1.f;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          if (r == n0) a0 = alpha[r];
+          if (r == n0 + 1) a1 = alpha[r];
+        }
+        uint32_t b0, b1;
+        ldsm_x2_trans(pw_addr, b0, b1);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          acc[mt][0] *= a0; acc[mt][1] *= a1; acc[mt][2] *= a0; acc[mt][3] *= a1;
+          uint32_t x0, x1, x2, x3;
+          ldsm_x4_trans(vtile_addr(vbase, vrows, vtok + kk_off, mt * 16 + dim_off), x0, x1, x2, x3);
+          mma_16816(acc[mt], x0, x1, x2, x3, b0, b1);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty_bar[s]);
+    }
+
+    // ---------------------------------------------- merge the warps of this CTA
+    float l_w[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      float v = l_l[r];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      l_w[r] = v;
+    }
+    named_bar_sync(1, kConsumers);  // every warp is done with the LUT: reuse it as scratch
+    float* wo = lut;                                  // [8][R][D]
+    float* wm = lut + kConsumerWarps * R * D;         // [8][R]
+    float* wl = wm + kConsumerWarps * R;              // [8][R]
+    {
+      const int n0 = 2 * (lane & 3);
+      const int m0 = lane >> 2;
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        if (n0 < R) {
+          wo[(warp * R + n0) * D + mt * 16 + m0] = acc[mt][0];
+          wo[(warp * R + n0) * D + mt * 16 + m0 + 8] = acc[mt][2];
+        }
+        if (n0 + 1 < R) {
+          wo[(warp * R + n0 + 1) * D + mt * 16 + m0] = acc[mt][1];
+          wo[(warp * R + n0 + 1) * D + mt * 16 + m0 + 8] = acc[mt][3];
+        }
+      }
+      if (lane == 0) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) { wm[warp * R + r] = m_w[r]; wl[warp * R + r] = l_w[r]; }
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty_bar[s]);
+    if (ctid == 0) ms.is_last = 0;
+    named_bar_sync(1, kConsumers);
+    for (int e = ctid; e < R * D; e += kConsumers) {
+      const int r = e / D, j = e - r * D;
+      float mstar = -INFINITY;
+      for (int w = 0; w < kConsumerWarps; ++w) mstar = fmaxf(mstar, wm[w * R + r]);
+      float O = 0.f, L = 0.f;
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        const float mg = wm[w * R + r];
+        const float wt = (mg == -INFINITY) ? 0.f : exp2f((mg - mstar) * kLog2e);
+        O = fmaf(wo[(w * R + r) * D + j], wt, O);
+        L = fmaf(wl[w * R + r], wt, L);
+      }
+      ms.o[r][j] = O;
+      if (j == 0) { ms.mrow[r] = mstar; ms.lrow[r] = L; }
+    }
+    named_bar_sync(1, kConsumers);
 
     // ---------------------------------------------- unit finalisation
-    const bool unit_end = (tau + 1 == t_end) || ((tau + 1) / p.tpu != u);
-    if (!unit_end) continue;
-
     const int64_t first = cta_of(u * p.tpu, p.total_tiles, p.grid);
     const int64_t last = cta_of((u + 1) * p.tpu - 1, p.total_tiles, p.grid);
     const int ncov = static_cast<int>(last - first + 1);
-    // stage o (unnormalised) into shared memory
-    if (mma_warp) {
-      const int m0 = mw * 16 + (lane >> 2);
-      const int n0 = 2 * (lane & 3);
-      if (n0 < R) { ms.o[n0][m0] = acc[0]; ms.o[n0][m0 + 8] = acc[2]; }
-      if (n0 + 1 < R) { ms.o[n0 + 1][m0] = acc[1]; ms.o[n0 + 1][m0 + 8] = acc[3]; }
-    }
-    if (ctid == 0) {
-      ms.is_last = 0;
-#pragma unroll
-      for (int r = 0; r < R; ++r) { ms.mrow[r] = m_run[r]; ms.lrow[r] = l_run[r]; }
-    }
-    named_bar_sync(1, kConsumers);
     const int row_floats = D + 2;
     bool do_final = true;
     if (ncov > 1) {
@@ -563,32 +598,22 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
       do_final = ms.is_last != 0;
       if (do_final) {
         __threadfence();
-        // merge all partial slots of this unit into ms.o / m_run / l_run
         const float* base = p.slots + (size_t)u * p.max_cov * R * row_floats;
-#pragma unroll 1
-        for (int r = 0; r < R; ++r) {
+        for (int e = ctid; e < R * D; e += kConsumers) {
+          const int r = e / D, j = e - r * D;
           float mstar = -INFINITY;
           for (int g = 0; g < ncov; ++g)
             mstar = fmaxf(mstar, __ldcg(base + ((size_t)g * R + r) * row_floats + D));
-          float L = 0.f;
+          float O = 0.f, L = 0.f;
           for (int g = 0; g < ncov; ++g) {
             const float* row = base + ((size_t)g * R + r) * row_floats;
             const float mg = __ldcg(row + D);
             const float w = (mg == -INFINITY) ? 0.f : exp2f((mg - mstar) * kLog2e);
-            L += __ldcg(row + D + 1) * w;
+            O = fmaf(__ldcg(row + j), w, O);
+            L = fmaf(__ldcg(row + D + 1), w, L);
           }
-          named_bar_sync(1, kConsumers);
-          for (int j = ctid; j < D; j += kConsumers) {
-            float O = 0.f;
-            for (int g = 0; g < ncov; ++g) {
-              const float* row = base + ((size_t)g * R + r) * row_floats;
-              const float mg = __ldcg(row + D);
-              const float w = (mg == -INFINITY) ? 0.f : exp2f((mg - mstar) * kLog2e);
-              O = fmaf(__ldcg(row + j), w, O);
-            }
-            ms.o[r][j] = O;
-          }
-          if (ctid == 0) { ms.mrow[r] = mstar; ms.lrow[r] = L; }
+          ms.o[r][j] = O;
+          if (j == 0) { ms.mrow[r] = mstar; ms.lrow[r] = L; }
         }
         named_bar_sync(1, kConsumers);
       }
@@ -597,7 +622,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
       for (int e = ctid; e < R * D; e += kConsumers) {
         const int r = e / D, j = e - r * D;
         const int rr = rg * R + r;
-        if (rr >= p.nrep * p.tq) continue;
+        if (rr >= rows_valid) continue;
         const int rep = rr / p.tq, tqi = rr - rep * p.tq;
         const int qh = hh * p.nrep + rep;
         if (p.part_out) {
@@ -618,7 +643,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
         }
       }
     }
-    named_bar_sync(1, kConsumers);
+    tau = u_end;
   }
 }
 
@@ -685,8 +710,7 @@ int make_plan(const ss_decode_args* a, Plan& pl) {
   while (R > 1 && (size_t)nb * a->k * R * 4 > 128 * 1024) R >>= 1;
   pl.R = R;
   pl.tile = R <= 4 ? 128 : 64;
-  const int TPT = kConsumers / pl.tile;
-  SS_REQUIRE(nb % TPT == 0, "ss_decode_attn: n_blocks must be a multiple of 4");
+  SS_REQUIRE(nb % 2 == 0 && nb <= 128, "ss_decode_attn: n_blocks must be even and <= 128");
   pl.n_rg = (rows + R - 1) / R;
   pl.n_ct = static_cast<int>((a->tc + pl.tile - 1) / pl.tile);
   pl.n_tt = static_cast<int>((a->ttail + pl.tile - 1) / pl.tile);
@@ -725,9 +749,13 @@ int make_plan(const ss_decode_args* a, Plan& pl) {
   aux += T * a->n_heavy * a->bd * 2;
   pl.stage_bytes = (pl.off_aux + aux + 1023) & ~1023u;
   size_t fixed = 0;
-  const size_t vdq = (a->vfmt == SS_V_QUANT) ? (size_t)T * a->d * 2 : 0;
-  const size_t lut = (size_t)nb * a->k * R * 4;
-  const size_t pbytes = (size_t)T * 16;
+  // per-warp fp16 value slices (16 tokens) for the quantized path
+  const size_t vdq = (a->vfmt == SS_V_QUANT) ? (size_t)kConsumerWarps * 16 * a->d * 2 : 0;
+  // the LUT region doubles as the per-warp merge scratch at unit ends
+  size_t lut = (size_t)nb * a->k * R * 4;
+  const size_t scratch = (size_t)kConsumerWarps * R * (a->d + 2) * 4;
+  if (lut < scratch) lut = scratch;
+  const size_t pbytes = (size_t)kConsumerWarps * 16 * 16;
   fixed = vdq + ((lut + 127) & ~size_t(127)) + pbytes + ((sizeof(Misc) + 127) & ~size_t(127)) + 1024;
   if (fixed + 2 * (size_t)pl.stage_bytes > kSmemBudget)
     return fail(SS_ERR_UNSUPPORTED, "ss_decode_attn: configuration exceeds shared memory");
