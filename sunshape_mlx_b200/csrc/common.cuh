@@ -90,14 +90,16 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+// One potentially-blocking probe of a barrier phase: the warp may be
+// suspended for up to ~0.5 ms waiting for the phase instead of spinning.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n .reg .pred p;\n"
-      " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
       " selp.u32 %0, 1, 0, p;\n}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(500000u)
       : "memory");
   return ok != 0;
 }
@@ -112,9 +114,9 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
                                                   uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
-  for (uint32_t i = 1;; ++i) {
+  for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0 && global_ns() - t0 > limit_ns) return false;
+    if (global_ns() - t0 > limit_ns) return false;
   }
 }
 

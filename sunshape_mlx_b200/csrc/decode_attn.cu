@@ -93,6 +93,17 @@ struct DecodeParams {
   uint32_t off_stage, stage_bytes, off_idx, off_aux, off_vdq, off_lut, off_p, off_misc;
 };
 
+// Tokens per consumer-warp slice (one per lane). With 128-token tiles this
+// gives two tile groups of four warps, so four stages double-buffer each group.
+__host__ __device__ constexpr int slice_tokens(int) { return 32; }
+
+// 2^x with the SFU approximation (ex2.approx.ftz): |rel err| < 2^-22.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ int64_t cta_of(int64_t tile, int64_t total, int grid) {
   return ((tile + 1) * grid - 1) / total;
 }
@@ -120,19 +131,65 @@ struct Misc {  // small shared-memory state
   int abort;
 };
 
+// Query x centroid table of one unit: lut[b][c][r] = <qc_r,b , C[b][c]>.
+// Thread t owns block b = t % nb (its R query sub-vectors stay in registers)
+// and centroids c = t / nb + i * (256 / nb); centroid rows are read as
+// 16-byte vectors. Heavy blocks scored from their fp16 values get zeros.
+template <int R, int BD>
+__device__ __forceinline__ void build_lut(const DecodeParams& p, const Misc& ms, float* lut,
+                                          int ctid) {
+  const int nb = p.nb;
+  const int b = ctid % nb;
+  const int c0 = ctid / nb, cstep = kConsumers / nb;
+  const bool zero = p.n_heavy > 0 && ms.is_heavy[b];
+  float q[R][BD];
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int j = 0; j < BD; ++j) q[r][j] = ms.qc[r][b * BD + j];
+  const float* cb = p.cents + (size_t)b * p.k * BD;
+  float* lb = lut + (size_t)b * p.k * R;
+#pragma unroll 4
+  for (int c = c0; c < p.k; c += cstep) {
+    float cv[BD];
+#pragma unroll
+    for (int j = 0; j < BD; j += 4) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(cb + (size_t)c * BD + j));
+      cv[j] = v.x; cv[j + 1] = v.y; cv[j + 2] = v.z; cv[j + 3] = v.w;
+    }
+    float o[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      float a = 0.f;
+#pragma unroll
+      for (int j = 0; j < BD; ++j) a = fmaf(q[r][j], cv[j], a);
+      o[r] = zero ? 0.f : a;
+    }
+    float* dst = lb + (size_t)c * R;
+    if constexpr (R % 4 == 0) {
+#pragma unroll
+      for (int r = 0; r < R; r += 4)
+        *reinterpret_cast<float4*>(dst + r) = make_float4(o[r], o[r + 1], o[r + 2], o[r + 3]);
+    } else {
+#pragma unroll
+      for (int r = 0; r < R; ++r) dst[r] = o[r];
+    }
+  }
+}
+
 template <int R, int D>
 __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
     const __grid_constant__ DecodeParams p, const __grid_constant__ CUtensorMap map_v,
     const __grid_constant__ CUtensorMap map_vt) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // Align to 1024 B (128-byte-swizzle atoms) by an offset from the __shared__
+  // array itself, so every access below stays a shared-memory access.
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   __shared__ uint64_t full_bar[kMaxStages], empty_bar[kMaxStages];
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int TILE = p.tile;
-  const int wpt = TILE / 16;                   // warps sharing one tile (16 tokens each)
   Misc& ms = *reinterpret_cast<Misc*>(smem + p.off_misc);
   float* lut = reinterpret_cast<float*>(smem + p.off_lut);
 
@@ -143,7 +200,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
   if (tid == 0) {
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], wpt);
+      mbar_init(&empty_bar[s], TILE / slice_tokens(R));
     }
     ms.abort = 0;
     int hp = 0;
@@ -241,23 +298,28 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
   }
 
   // ====================================================== consumer warps
-  // Warp w owns 16-token slice (w % wpt) of every tile of tile group (w / wpt);
-  // two lanes per token, each summing half of the blocks.
+  // Warp w owns 64-token slice (w % wps) of every tile of its tile group
+  // (w / wps); lane l scores tokens l and l + 32 of the slice over all blocks.
   constexpr int MT = D / 16;                   // 16-dim MMA tiles of the output
-  const int tgroups = kConsumerWarps / wpt;
-  const int wgroup = warp / wpt, slice = warp % wpt;
-  const int ltok = lane >> 1, part = lane & 1;
-  const int tok = slice * 16 + ltok;           // token within the tile
-  const int nbp = p.nb / 2;
+  constexpr int TPL = slice_tokens(R) / 32;    // tokens per lane
+  constexpr int SL = 32 * TPL;                 // tokens per warp slice
+  const int wps = TILE / SL;                   // warps sharing one tile
+  const int tgroups = kConsumerWarps / wps;
+  const int wgroup = warp / wps, slice = warp % wps;
   const int ctid = tid;                        // 0..255
   const int64_t q_off = p.tc + p.ttail - p.tq;
-  __half* Pw = reinterpret_cast<__half*>(smem + p.off_p) + warp * 16 * 8;  // [16][8]
+  __half* Pw = reinterpret_cast<__half*>(smem + p.off_p) + warp * SL * 8;  // [64][8]
   uint8_t* vdq_w = smem + p.off_vdq + warp * (16 * D * 2);
   const uint32_t pw_addr = smem_u32(Pw) + (lane & 15) * 16;
+  // ldmatrix.x4.trans addressing: lane -> (8x8 matrix mi, row mj)
   const int mi = lane >> 3, mj = lane & 7;
-  const int kk_off = (mi >= 2 ? 8 : 0) + mj;   // ldmatrix row (token) of this lane
-  const int dim_off = (mi & 1) ? 8 : 0;
+  const int kk_off = (mi >= 2 ? 8 : 0) + mj;   // token row within a 16-token k-step
+  const int dsel = mi & 1;                     // second 8-dim half of the 16-dim tile
   const int rows_valid = p.nrep * p.tq;
+  const bool per_token_mask = p.causal || p.mask != nullptr;
+  // columns R..7 of every P slice stay zero
+  for (int e = lane; e < SL * 8; e += 32)
+    if ((e & 7) >= R) Pw[e] = __float2half_rn(0.f);
 
   int64_t tau = t_begin;
   while (tau < t_end) {
@@ -297,23 +359,34 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
         ms.qc[r][j] = v;
       }
       named_bar_sync(1, kConsumers);
-      for (int e = ctid; e < p.nb * p.k; e += kConsumers) {
-        const int b = e / p.k;
-        const float* c = p.cents + (size_t)e * p.bd;
-        // Heavy blocks are scored exactly from their fp16 values when the
-        // cache stores them (n_heavy > 0); their table entries are zero then.
-        const bool zero = p.n_heavy > 0 && ms.is_heavy[b];
-        float cv[16];
-        for (int j = 0; j < p.bd; ++j) cv[j] = zero ? 0.f : __ldg(c + j);
-        float* dst = lut + (size_t)e * R;
+      if (p.bd == 8 && kConsumers % p.nb == 0) {
+        build_lut<R, 8>(p, ms, lut, ctid);
+      } else if (p.bd == 4 && kConsumers % p.nb == 0) {
+        build_lut<R, 4>(p, ms, lut, ctid);
+      } else {
+        for (int e = ctid; e < p.nb * p.k; e += kConsumers) {
+          const int b = e / p.k;
+          const float* c = p.cents + (size_t)e * p.bd;
+          const bool zero = p.n_heavy > 0 && ms.is_heavy[b];
+          float* dst = lut + (size_t)e * R;
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
-          float a = 0.f;
-          for (int j = 0; j < p.bd; ++j) a = fmaf(ms.qc[r][b * p.bd + j], cv[j], a);
-          dst[r] = a;
+          for (int r = 0; r < R; ++r) {
+            float a = 0.f;
+            for (int j = 0; j < p.bd; ++j) a = fmaf(ms.qc[r][b * p.bd + j], __ldg(c + j), a);
+            dst[r] = zero ? 0.f : a;
+          }
         }
       }
       named_bar_sync(1, kConsumers);
+    }
+    // per-row constants of this unit
+    int tq_r[R];
+    bool rok[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int rr = rg * R + r;
+      rok[r] = rr < rows_valid;
+      tq_r[r] = rr % p.tq;
     }
 
     // ---------------------------------------------- this warp's slices of the unit
@@ -337,170 +410,140 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
       uint8_t* st = smem + (size_t)s * p.stage_bytes;
       const bool compressed = lt < p.n_ct;
       const int64_t t0 = compressed ? (int64_t)lt * TILE : (int64_t)(lt - p.n_ct) * TILE;
-      const int64_t len = compressed ? p.tc : p.ttail;
-      const int64_t t = t0 + tok;
-      const bool tvalid = t < len && !aborted;
-      const int64_t tg = compressed ? t : p.tc + t;
+      const int64_t rem_ = (compressed ? p.tc : p.ttail) - t0;
+      const int len = static_cast<int>(rem_ < TILE ? rem_ : TILE);
+      const int tok0 = slice * SL + lane;       // tokens of this lane within the tile
+      const int tok1 = TPL > 1 ? tok0 + 32 : tok0;
+      const bool v0 = tok0 < len && !aborted, v1 = TPL > 1 && tok1 < len && !aborted;
 
-      // 1. scores of this lane's token (half of the blocks)
-      float sc[R];
+      // 1. scores
+      float s0[R], s1[R];
 #pragma unroll
-      for (int r = 0; r < R; ++r) sc[r] = 0.f;
-      if (tvalid) {
-        if (compressed) {
-          const uint8_t* irow = st + p.off_idx + tok * p.nb + part * nbp;
-          for (int j0 = 0; j0 < nbp; j0 += 8) {
-            const uint2 raw = *reinterpret_cast<const uint2*>(irow + j0);
-            const uint32_t w2[2] = {raw.x, raw.y};
+      for (int r = 0; r < R; ++r) { s0[r] = 0.f; s1[r] = 0.f; }
+      if (compressed) {
+        const uint8_t* ir0 = st + p.off_idx + tok0 * p.nb;
+        const uint8_t* ir1 = st + p.off_idx + tok1 * p.nb;
+        if ((p.nb & 3) == 0) {
+          for (int w = 0; w < (p.nb >> 2); ++w) {
+            const uint32_t c0w = v0 ? reinterpret_cast<const uint32_t*>(ir0)[w] : 0u;
+            const uint32_t c1w = v1 ? reinterpret_cast<const uint32_t*>(ir1)[w] : 0u;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              if (j0 + j >= nbp) break;
-              const int b = part * nbp + j0 + j;
-              const uint32_t c = (w2[j >> 2] >> ((j & 3) * 8)) & 0xffu;
-              const float* e = lut + ((size_t)b * p.k + c) * R;
-              if constexpr (R == 4) {
-                const float4 v = *reinterpret_cast<const float4*>(e);
-                sc[0] += v.x; sc[1] += v.y; sc[2] += v.z; sc[3] += v.w;
-              } else if constexpr (R == 8) {
-                const float4 v0 = *reinterpret_cast<const float4*>(e);
-                const float4 v1 = *reinterpret_cast<const float4*>(e + 4);
-                sc[0] += v0.x; sc[1] += v0.y; sc[2] += v0.z; sc[3] += v0.w;
-                sc[4] += v1.x; sc[5] += v1.y; sc[6] += v1.z; sc[7] += v1.w;
+            for (int j = 0; j < 4; ++j) {
+              const int b = 4 * w + j;
+              const float* e0 = lut + ((size_t)b * p.k + ((c0w >> (8 * j)) & 0xffu)) * R;
+              const float* e1 = lut + ((size_t)b * p.k + ((c1w >> (8 * j)) & 0xffu)) * R;
+              if constexpr (R % 4 == 0) {
+#pragma unroll
+                for (int r4 = 0; r4 < R; r4 += 4) {
+                  const float4 a4 = *reinterpret_cast<const float4*>(e0 + r4);
+                  const float4 b4 = *reinterpret_cast<const float4*>(e1 + r4);
+                  s0[r4] += a4.x; s0[r4 + 1] += a4.y; s0[r4 + 2] += a4.z; s0[r4 + 3] += a4.w;
+                  s1[r4] += b4.x; s1[r4 + 1] += b4.y; s1[r4 + 2] += b4.z; s1[r4 + 3] += b4.w;
+                }
               } else {
 #pragma unroll
-                for (int r = 0; r < R; ++r) sc[r] += e[r];
-              }
-            }
-          }
-          if (p.n_heavy) {
-            int off = p.off_aux;
-            if (p.vfmt != SS_V_F16) {
-              off += TILE * p.v_words * 4 + TILE * p.v_groups * (p.vs_dt == SS_F32 ? 4 : 2);
-              if (p.vz) off += TILE * p.v_groups * 4;
-            }
-            const uint16_t* hrow =
-                reinterpret_cast<const uint16_t*>(st + off) + (size_t)tok * p.n_heavy * p.bd;
-            for (int hj = part; hj < p.n_heavy; hj += 2) {
-              const int b = ms.heavy_pos[hj];
-              for (int j = 0; j < p.bd; ++j) {
-                const float kv = h2f(hrow[hj * p.bd + j]);
-#pragma unroll
-                for (int r = 0; r < R; ++r) sc[r] = fmaf(ms.qc[r][b * p.bd + j], kv, sc[r]);
+                for (int r = 0; r < R; ++r) { s0[r] += e0[r]; s1[r] += e1[r]; }
               }
             }
           }
         } else {
-          const uint16_t* krow = p.k_tail + pair * p.tail_ps + t * D;
-          constexpr int per = D / 2;
-          for (int j0 = part * per; j0 < (part + 1) * per; j0 += 8) {
-            const uint4 raw = *reinterpret_cast<const uint4*>(krow + j0);
-            const uint16_t* hv = reinterpret_cast<const uint16_t*>(&raw);
+          for (int b = 0; b < p.nb; ++b) {
+            const float* e0 = lut + ((size_t)b * p.k + (v0 ? ir0[b] : 0)) * R;
+            const float* e1 = lut + ((size_t)b * p.k + (v1 ? ir1[b] : 0)) * R;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float kv = h2f(hv[j]);
+            for (int r = 0; r < R; ++r) { s0[r] += e0[r]; s1[r] += e1[r]; }
+          }
+        }
+        if (p.n_heavy) {
+          int off = p.off_aux;
+          if (p.vfmt != SS_V_F16) {
+            off += TILE * p.v_words * 4 + TILE * p.v_groups * (p.vs_dt == SS_F32 ? 4 : 2);
+            if (p.vz) off += TILE * p.v_groups * 4;
+          }
+          const uint16_t* h0 = reinterpret_cast<const uint16_t*>(st + off) + (size_t)tok0 * p.n_heavy * p.bd;
+          const uint16_t* h1 = reinterpret_cast<const uint16_t*>(st + off) + (size_t)tok1 * p.n_heavy * p.bd;
+          for (int hj = 0; hj < p.n_heavy; ++hj) {
+            const int b = ms.heavy_pos[hj];
+            for (int j = 0; j < p.bd; ++j) {
+              const float k0 = h2f(h0[hj * p.bd + j]), k1 = h2f(h1[hj * p.bd + j]);
 #pragma unroll
-              for (int r = 0; r < R; ++r) sc[r] = fmaf(ms.qo[r][j0 + j], kv, sc[r]);
+              for (int r = 0; r < R; ++r) {
+                const float qv = ms.qc[r][b * p.bd + j];
+                s0[r] = fmaf(qv, k0, s0[r]);
+                s1[r] = fmaf(qv, k1, s1[r]);
+              }
+            }
+          }
+        }
+      } else {
+        const uint16_t* kr0 = p.k_tail + pair * p.tail_ps + (t0 + tok0) * D;
+        const uint16_t* kr1 = p.k_tail + pair * p.tail_ps + (t0 + tok1) * D;
+        for (int j0 = 0; j0 < D; j0 += 8) {
+          const uint4 a0 = v0 ? *reinterpret_cast<const uint4*>(kr0 + j0) : make_uint4(0, 0, 0, 0);
+          const uint4 a1 = v1 ? *reinterpret_cast<const uint4*>(kr1 + j0) : make_uint4(0, 0, 0, 0);
+          const uint16_t* x0 = reinterpret_cast<const uint16_t*>(&a0);
+          const uint16_t* x1 = reinterpret_cast<const uint16_t*>(&a1);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float k0 = h2f(x0[j]), k1 = h2f(x1[j]);
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+              const float qv = ms.qo[r][j0 + j];
+              s0[r] = fmaf(qv, k0, s0[r]);
+              s1[r] = fmaf(qv, k1, s1[r]);
             }
           }
         }
       }
-#pragma unroll
-      for (int r = 0; r < R; ++r) sc[r] += __shfl_xor_sync(0xffffffffu, sc[r], 1);
+      // masking: invalid tokens / rows -> -inf; causal; mask arrays
+      const int64_t tg0 = (compressed ? t0 : p.tc + t0) + tok0;
+      const int64_t tg1 = tg0 + 32;
 #pragma unroll
       for (int r = 0; r < R; ++r) {
-        const int rr = rg * R + r;
-        bool ok = tvalid && rr < rows_valid;
-        const int tqi = rr % p.tq;
-        if (ok && p.causal && tg > q_off + tqi) ok = false;
-        if (ok && p.mask) {
-          const float mv = p.mask[tqi * p.mask_stride + tg];
-          if (p.mask_mode == 0) sc[r] += mv;
-          else if (mv == 0.f) sc[r] = -FLT_MAX;
+        bool ok0 = v0 && rok[r], ok1 = v1 && rok[r];
+        if (per_token_mask) {
+          if (p.causal) {
+            ok0 = ok0 && tg0 <= q_off + tq_r[r];
+            ok1 = ok1 && tg1 <= q_off + tq_r[r];
+          }
+          if (p.mask) {
+            const float* mrow = p.mask + tq_r[r] * p.mask_stride;
+            if (ok0) {
+              const float mv = mrow[tg0];
+              if (p.mask_mode == 0) s0[r] += mv; else if (mv == 0.f) s0[r] = -FLT_MAX;
+            }
+            if (ok1) {
+              const float mv = mrow[tg1];
+              if (p.mask_mode == 0) s1[r] += mv; else if (mv == 0.f) s1[r] = -FLT_MAX;
+            }
+          }
         }
-        if (!ok) sc[r] = -INFINITY;
+        if (!ok0) s0[r] = -INFINITY;
+        if (!ok1) s1[r] = -INFINITY;
       }
 
       // 2. online softmax over this warp's slice
       float alpha[R];
 #pragma unroll
       for (int r = 0; r < R; ++r) {
-        float mx = sc[r];
+        float mx = TPL > 1 ? fmaxf(s0[r], s1[r]) : s0[r];
 #pragma unroll
-        for (int o = 2; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        for (int o = 1; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         const float mn = fmaxf(m_w[r], mx);
-        alpha[r] = (mn == -INFINITY) ? 1.f : exp2f((m_w[r] - mn) * kLog2e);
-        const float e = (sc[r] == -INFINITY) ? 0.f : exp2f((sc[r] - mn) * kLog2e);
-        const __half h = __float2half_rn(e);
-        if (part == 0) {
-          Pw[ltok * 8 + r] = h;
-          l_l[r] = l_l[r] * alpha[r] + __half2float(h);
+        float p0 = 0.f, p1 = 0.f;
+        if (mn == -INFINITY) {
+          alpha[r] = 1.f;
         } else {
-          l_l[r] *= alpha[r];
+          alpha[r] = fast_exp2((m_w[r] - mn) * kLog2e);
+          p0 = fast_exp2((s0[r] - mn) * kLog2e);
+          p1 = fast_exp2((s1[r] - mn) * kLog2e);
         }
+        const __half h0 = __float2half_rn(p0), h1 = __float2half_rn(p1);
+        Pw[lane * 8 + r] = h0;
+        if (TPL > 1) Pw[(lane + 32) * 8 + r] = h1;
+        l_l[r] = l_l[r] * alpha[r] + (__half2float(h0) + (TPL > 1 ? __half2float(h1) : 0.f));
         m_w[r] = mn;
       }
-      if (part == 0) {
-#pragma unroll
-        for (int r = R; r < 8; ++r) Pw[ltok * 8 + r] = __float2half_rn(0.f);
-      }
-
-      // quantized values (or the quantized path's tail) -> this warp's fp16 slice
-      uint32_t vbase;
-      int vrows, vtok;
-      if (p.vfmt == SS_V_F16) {
-        vbase = smem_u32(st);
-        vrows = TILE;
-        vtok = slice * 16;
-      } else {
-        vbase = smem_u32(vdq_w);
-        vrows = 16;
-        vtok = 0;
-        if (compressed) {
-          const uint32_t* words = reinterpret_cast<const uint32_t*>(st + p.off_aux);
-          const uint8_t* sp = st + p.off_aux + TILE * p.v_words * 4;
-          const float* zp = p.vz ? reinterpret_cast<const float*>(
-                                       sp + TILE * p.v_groups * (p.vs_dt == SS_F32 ? 4 : 2))
-                                 : nullptr;
-          const int vpw = p.v_bits == 3 ? 10 : 32 / p.v_bits;
-          const uint32_t msk = (1u << p.v_bits) - 1u;
-          for (int e = lane; e < 16 * (D / 8); e += 32) {
-            const int tk = e / (D / 8), ch = e - tk * (D / 8);
-            const int tt = slice * 16 + tk;
-            const int gi = (ch * 8) / p.v_group;
-            const float s_ = p.vs_dt == SS_F32
-                                 ? reinterpret_cast<const float*>(sp)[tt * p.v_groups + gi]
-                                 : h2f(reinterpret_cast<const uint16_t*>(sp)[tt * p.v_groups + gi]);
-            const float z_ = zp ? zp[tt * p.v_groups + gi] : 0.f;
-            float vals[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const int c = ch * 8 + j;
-              const uint32_t code = (words[tt * p.v_words + c / vpw] >> ((c % vpw) * p.v_bits)) & msk;
-              float x = __fmul_rn(ms.levels[code], s_);
-              if (zp) x = __fadd_rn(x, z_);
-              vals[j] = x;
-            }
-            uint4 pk;
-            pk.x = pack_h2(vals[0], vals[1]);
-            pk.y = pack_h2(vals[2], vals[3]);
-            pk.z = pack_h2(vals[4], vals[5]);
-            pk.w = pack_h2(vals[6], vals[7]);
-            *reinterpret_cast<uint4*>(vdq_w + vtile_addr(0, 16, tk, ch * 8)) = pk;
-          }
-        } else {
-          for (int e = lane; e < 16 * (D / 8); e += 32) {
-            const int tk = e / (D / 8), ch = e - tk * (D / 8);
-            const int64_t tt = t0 + slice * 16 + tk;
-            uint4 pk = make_uint4(0, 0, 0, 0);
-            if (tt < len)
-              pk = *reinterpret_cast<const uint4*>(p.v_tail + pair * p.tail_ps + tt * D + ch * 8);
-            *reinterpret_cast<uint4*>(vdq_w + vtile_addr(0, 16, tk, ch * 8)) = pk;
-          }
-        }
-      }
-      __syncwarp();
-
-      // 3. P.V: O^T[dims][rows] += V^T[dims][16 tokens] . P[16 tokens][rows]
       {
         const int n0 = 2 * (lane & 3);
         float a0 = 1.f, a1 = 1.f;
@@ -509,14 +552,85 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
           if (r == n0) a0 = alpha[r];
           if (r == n0 + 1) a1 = alpha[r];
         }
-        uint32_t b0, b1;
-        ldsm_x2_trans(pw_addr, b0, b1);
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
           acc[mt][0] *= a0; acc[mt][1] *= a1; acc[mt][2] *= a0; acc[mt][3] *= a1;
-          uint32_t x0, x1, x2, x3;
-          ldsm_x4_trans(vtile_addr(vbase, vrows, vtok + kk_off, mt * 16 + dim_off), x0, x1, x2, x3);
-          mma_16816(acc[mt], x0, x1, x2, x3, b0, b1);
+        }
+      }
+      __syncwarp();
+
+      // 3. P.V: O^T[dims][rows] += V^T[dims][64 tokens] . P[64 tokens][rows]
+      if (p.vfmt == SS_V_F16) {
+        const uint32_t vb = smem_u32(st) + (slice * SL + kk_off) * 128;
+#pragma unroll
+        for (int ks = 0; ks < SL / 16; ++ks) {
+          uint32_t b0, b1;
+          ldsm_x2_trans(pw_addr + ks * 256, b0, b1);
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            const uint32_t col = (mt >> 2) * (TILE * 128) + ((((2 * mt + dsel) & 7) ^ mj) << 4);
+            uint32_t x0, x1, x2, x3;
+            ldsm_x4_trans(vb + ks * 2048 + col, x0, x1, x2, x3);
+            mma_16816(acc[mt], x0, x1, x2, x3, b0, b1);
+          }
+        }
+      } else {
+        const uint32_t vb = smem_u32(vdq_w) + kk_off * 128;
+        for (int ks = 0; ks < SL / 16; ++ks) {
+          // decode 16 tokens of the slice into this warp's fp16 staging tile
+          if (compressed) {
+            const uint32_t* words = reinterpret_cast<const uint32_t*>(st + p.off_aux);
+            const uint8_t* sp = st + p.off_aux + TILE * p.v_words * 4;
+            const float* zp = p.vz ? reinterpret_cast<const float*>(
+                                         sp + TILE * p.v_groups * (p.vs_dt == SS_F32 ? 4 : 2))
+                                   : nullptr;
+            const int vpw = p.v_bits == 3 ? 10 : 32 / p.v_bits;
+            const uint32_t msk = (1u << p.v_bits) - 1u;
+            for (int e = lane; e < 16 * (D / 8); e += 32) {
+              const int tk = e / (D / 8), ch = e - tk * (D / 8);
+              const int tt = slice * SL + ks * 16 + tk;
+              const int gi = (ch * 8) / p.v_group;
+              const float s_ = p.vs_dt == SS_F32
+                                   ? reinterpret_cast<const float*>(sp)[tt * p.v_groups + gi]
+                                   : h2f(reinterpret_cast<const uint16_t*>(sp)[tt * p.v_groups + gi]);
+              const float z_ = zp ? zp[tt * p.v_groups + gi] : 0.f;
+              float vals[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const int c = ch * 8 + j;
+                const uint32_t code = (words[tt * p.v_words + c / vpw] >> ((c % vpw) * p.v_bits)) & msk;
+                float x = __fmul_rn(ms.levels[code], s_);
+                if (zp) x = __fadd_rn(x, z_);
+                vals[j] = x;
+              }
+              uint4 pk;
+              pk.x = pack_h2(vals[0], vals[1]);
+              pk.y = pack_h2(vals[2], vals[3]);
+              pk.z = pack_h2(vals[4], vals[5]);
+              pk.w = pack_h2(vals[6], vals[7]);
+              *reinterpret_cast<uint4*>(vdq_w + vtile_addr(0, 16, tk, ch * 8)) = pk;
+            }
+          } else {
+            for (int e = lane; e < 16 * (D / 8); e += 32) {
+              const int tk = e / (D / 8), ch = e - tk * (D / 8);
+              const int tt = slice * SL + ks * 16 + tk;
+              uint4 pk = make_uint4(0, 0, 0, 0);
+              if (tt < len)
+                pk = *reinterpret_cast<const uint4*>(p.v_tail + pair * p.tail_ps + (t0 + tt) * D + ch * 8);
+              *reinterpret_cast<uint4*>(vdq_w + vtile_addr(0, 16, tk, ch * 8)) = pk;
+            }
+          }
+          __syncwarp();
+          uint32_t b0, b1;
+          ldsm_x2_trans(pw_addr + ks * 256, b0, b1);
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            const uint32_t col = (mt >> 2) * (16 * 128) + ((((2 * mt + dsel) & 7) ^ mj) << 4);
+            uint32_t x0, x1, x2, x3;
+            ldsm_x4_trans(vb + col, x0, x1, x2, x3);
+            mma_16816(acc[mt], x0, x1, x2, x3, b0, b1);
+          }
+          __syncwarp();
         }
       }
       __syncwarp();
@@ -709,7 +823,7 @@ int make_plan(const ss_decode_args* a, Plan& pl) {
   int R = rows >= 5 ? 8 : (rows >= 3 ? 4 : (rows == 2 ? 2 : 1));
   while (R > 1 && (size_t)nb * a->k * R * 4 > 128 * 1024) R >>= 1;
   pl.R = R;
-  pl.tile = R <= 4 ? 128 : 64;
+  pl.tile = 128;
   SS_REQUIRE(nb % 2 == 0 && nb <= 128, "ss_decode_attn: n_blocks must be even and <= 128");
   pl.n_rg = (rows + R - 1) / R;
   pl.n_ct = static_cast<int>((a->tc + pl.tile - 1) / pl.tile);
@@ -755,12 +869,19 @@ int make_plan(const ss_decode_args* a, Plan& pl) {
   size_t lut = (size_t)nb * a->k * R * 4;
   const size_t scratch = (size_t)kConsumerWarps * R * (a->d + 2) * 4;
   if (lut < scratch) lut = scratch;
-  const size_t pbytes = (size_t)kConsumerWarps * 16 * 16;
+  const size_t pbytes = (size_t)kConsumerWarps * 64 * 16;
   fixed = vdq + ((lut + 127) & ~size_t(127)) + pbytes + ((sizeof(Misc) + 127) & ~size_t(127)) + 1024;
   if (fixed + 2 * (size_t)pl.stage_bytes > kSmemBudget)
     return fail(SS_ERR_UNSUPPORTED, "ss_decode_attn: configuration exceeds shared memory");
   int stages = static_cast<int>((kSmemBudget - fixed) / pl.stage_bytes);
   if (stages > 4) stages = 4;
+  // The consumer warps form tile groups that take tiles round robin; a warp may
+  // only wait for the barrier phase right after the one it consumed last,
+  // which holds when the stage count is a multiple of the number of groups.
+  const int tgroups = slice_tokens(R) / 16;  // = consumer warps / warps per tile
+  stages -= stages % tgroups;
+  if (stages < tgroups)
+    return fail(SS_ERR_UNSUPPORTED, "ss_decode_attn: configuration exceeds shared memory");
   pl.stages = stages;
   size_t off = (size_t)stages * pl.stage_bytes;
   pl.off_vdq = static_cast<uint32_t>(off);

