@@ -177,7 +177,7 @@ __device__ __forceinline__ void build_lut(const DecodeParams& p, const Misc& ms,
   }
 }
 
-template <int R, int D>
+template <int R, int D, int NBC>
 __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
     const __grid_constant__ DecodeParams p, const __grid_constant__ CUtensorMap map_v,
     const __grid_constant__ CUtensorMap map_vt) {
@@ -189,7 +189,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
-  const int TILE = p.tile;
+  constexpr int TILE = 128;
   Misc& ms = *reinterpret_cast<Misc*>(smem + p.off_misc);
   float* lut = reinterpret_cast<float*>(smem + p.off_lut);
 
@@ -423,26 +423,35 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
       if (compressed) {
         const uint8_t* ir0 = st + p.off_idx + tok0 * p.nb;
         const uint8_t* ir1 = st + p.off_idx + tok1 * p.nb;
-        if ((p.nb & 3) == 0) {
-          for (int w = 0; w < (p.nb >> 2); ++w) {
+        if (NBC > 0 || (p.nb & 3) == 0) {
+          const int nbw = NBC > 0 ? NBC / 4 : (p.nb >> 2);
+          const uint32_t kstride = static_cast<uint32_t>(p.k) * R;  // floats per block
+#pragma unroll
+          for (int w = 0; w < (NBC > 0 ? NBC / 4 : 32); ++w) {
+            if (NBC == 0 && w >= nbw) break;
             const uint32_t c0w = v0 ? reinterpret_cast<const uint32_t*>(ir0)[w] : 0u;
             const uint32_t c1w = v1 ? reinterpret_cast<const uint32_t*>(ir1)[w] : 0u;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              const int b = 4 * w + j;
-              const float* e0 = lut + ((size_t)b * p.k + ((c0w >> (8 * j)) & 0xffu)) * R;
-              const float* e1 = lut + ((size_t)b * p.k + ((c1w >> (8 * j)) & 0xffu)) * R;
+              const uint32_t bo = (4 * w + j) * kstride;
+              const float* e0 = lut + (bo + ((c0w >> (8 * j)) & 0xffu) * R);
+              const float* e1 = lut + (bo + ((c1w >> (8 * j)) & 0xffu) * R);
               if constexpr (R % 4 == 0) {
 #pragma unroll
                 for (int r4 = 0; r4 < R; r4 += 4) {
                   const float4 a4 = *reinterpret_cast<const float4*>(e0 + r4);
-                  const float4 b4 = *reinterpret_cast<const float4*>(e1 + r4);
                   s0[r4] += a4.x; s0[r4 + 1] += a4.y; s0[r4 + 2] += a4.z; s0[r4 + 3] += a4.w;
-                  s1[r4] += b4.x; s1[r4 + 1] += b4.y; s1[r4 + 2] += b4.z; s1[r4 + 3] += b4.w;
+                  if (TPL > 1) {
+                    const float4 b4 = *reinterpret_cast<const float4*>(e1 + r4);
+                    s1[r4] += b4.x; s1[r4 + 1] += b4.y; s1[r4 + 2] += b4.z; s1[r4 + 3] += b4.w;
+                  }
                 }
               } else {
 #pragma unroll
-                for (int r = 0; r < R; ++r) { s0[r] += e0[r]; s1[r] += e1[r]; }
+                for (int r = 0; r < R; ++r) {
+                  s0[r] += e0[r];
+                  if (TPL > 1) s1[r] += e1[r];
+                }
               }
             }
           }
@@ -903,7 +912,7 @@ int make_plan(const ss_decode_args* a, Plan& pl) {
 template <int R, int D>
 int launch_decode(const DecodeParams& p, const CUtensorMap& mv, const CUtensorMap& mvt,
                   size_t smem, cudaStream_t st) {
-  auto kern = decode_attn_kernel<R, D>;
+  auto kern = p.nb == 16 ? decode_attn_kernel<R, D, 16> : decode_attn_kernel<R, D, 0>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess)
