@@ -242,6 +242,20 @@ typedef struct ss_decode_args {
 
 size_t ss_decode_workspace_size(const ss_decode_args* a);
 int ss_decode_attn(const ss_decode_args* a, void* stream);
+/* ss_decode_attn for callers that cannot allocate device memory (runtimes
+ * without an allocator, code confined to another framework's memory pool,
+ * hosts that only pass pre-registered input/output buffers). No counterpart
+ * in the reference, which never manages device memory itself.
+ * Identical results to ss_decode_attn; a->workspace is ignored. The decode
+ * scratch is a fixed 8 MiB device array inside this library, held by every
+ * GPU that loads it until process exit; problems needing more scratch than
+ * ss_decode_workspace_size() allows there are rejected with SS_ERR_WORKSPACE.
+ * The first call on a device looks up the array's device address (make it
+ * before any stream capture). Every call shares the one array: calls that
+ * may overlap on the GPU (different streams, or threads) race. No memory is
+ * allocated or freed. */
+int ss_decode_attn_noalloc(const ss_decode_args* a, void* stream);
+
 /* Reads and clears the sticky device-side error word of a decode workspace
  * (synchronizes the stream). Returns SS_OK or SS_ERR_TIMEOUT. */
 int ss_decode_check(void* workspace, void* stream);

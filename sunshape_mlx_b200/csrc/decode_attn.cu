@@ -24,6 +24,8 @@
 // Quantized values are first decoded (levels * scale + zero) into an fp16
 // tile in the same swizzled layout and then take the same MMA path.
 #include <cfloat>
+#include <mutex>
+#include <string>
 
 #include "common.cuh"
 
@@ -1065,3 +1067,63 @@ int ss_lse_merge(const float* parts, int n_parts, int64_t rows, int d, const flo
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Decode attention without any allocation by the caller.
+//
+// Some callers cannot allocate device memory at the point where they run
+// attention: allocator-less runtimes, code running inside another
+// framework's memory pool that forbids extra cudaMalloc traffic, or hosts
+// that only hand over pre-registered input/output buffers. For them the
+// decode workspace (error word, per-unit arrival counters, cross-CTA partial
+// rows) lives in this fixed device array instead of a caller buffer.
+namespace {
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB per device
+static __device__ __align__(256) uint8_t g_decode_scratch[kNoAllocScratchBytes];
+
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[64] = {nullptr};
+
+// Device address of g_decode_scratch on the current device (looked up once).
+int scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(SS_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return fail(SS_ERR_UNSUPPORTED, "ss_decode_attn_noalloc: device index >= 64");
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  if (!g_scratch_ptr[dev]) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_decode_scratch);
+    if (e != cudaSuccess || !ptr)
+      return fail(SS_ERR_CUDA, std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e));
+    g_scratch_ptr[dev] = ptr;
+  }
+  *out = g_scratch_ptr[dev];
+  return SS_OK;
+}
+}  // namespace
+
+extern "C" int ss_decode_attn_noalloc(const ss_decode_args* a, void* stream) {
+  SS_REQUIRE(a, "ss_decode_attn_noalloc: null args");
+  Plan pl;
+  int rc = make_plan(a, pl);
+  if (rc != SS_OK) return rc;
+  if (pl.ws_bytes > kNoAllocScratchBytes)
+    return fail(SS_ERR_WORKSPACE,
+                "ss_decode_attn_noalloc: this problem needs " + std::to_string(pl.ws_bytes) +
+                    " bytes of decode scratch, more than the fixed " +
+                    std::to_string(kNoAllocScratchBytes) +
+                    " bytes; use ss_decode_attn with a caller workspace");
+  void* scratch = nullptr;
+  rc = scratch_address(&scratch);
+  if (rc != SS_OK) return rc;
+  // error word + arrival counters must start at zero; the array keeps the
+  // previous call's contents
+  cudaError_t e = cudaMemsetAsync(scratch, 0, pl.off_slots, as_stream(stream));
+  if (e != cudaSuccess)
+    return fail(SS_ERR_CUDA, std::string("ss_decode_attn_noalloc: memset: ") + cudaGetErrorString(e));
+  ss_decode_args b = *a;
+  b.workspace = scratch;
+  b.workspace_bytes = kNoAllocScratchBytes;
+  return run_decode(&b, nullptr, stream);
+}
