@@ -44,7 +44,7 @@ struct DecodeParams {
   int b, hq, hkv, tq, d, nb, bd, k, nrep, n_heavy;
   int R, tile, n_rg, n_ct, n_tt, tpu;
   int64_t tc, ttail, total_tiles, n_units;
-  int grid, stages, max_cov;
+  int grid, stages, stage_shift, max_cov;  // stages is a power of two
   // queries
   const void* q;
   int qdt;
@@ -222,19 +222,26 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
       if (p.vfmt == SS_V_F16 && p.n_ct > 0) prefetch_tmap(&map_v);
       if (p.n_tt > 0 && p.vfmt == SS_V_F16) prefetch_tmap(&map_vt);
       int it = 0;
+      // walk (unit, tile) incrementally: no per-tile 64-bit division
+      int64_t u = t_begin / p.tpu;
+      int lt = static_cast<int>(t_begin - u * p.tpu);
+      int64_t pair = u / p.n_rg;
+      int rgc = static_cast<int>(u - pair * p.n_rg);
       for (int64_t tau = t_begin; tau < t_end; ++tau, ++it) {
-        const int s = it % p.stages;
+        if (tau != t_begin && ++lt == p.tpu) {
+          lt = 0;
+          ++u;
+          if (++rgc == p.n_rg) { rgc = 0; ++pair; }
+        }
+        const int s = it & (p.stages - 1);
         if (it >= p.stages) {
-          if (ms.abort || !mbar_wait_bounded(&empty_bar[s], ((it / p.stages) - 1) & 1,
+          if (ms.abort || !mbar_wait_bounded(&empty_bar[s], ((it >> p.stage_shift) - 1) & 1,
                                              kWaitLimitNs)) {
             ms.abort = 1;
             atomicOr(p.err, 1);
             break;
           }
         }
-        const int64_t u = tau / p.tpu;
-        const int lt = static_cast<int>(tau - u * p.tpu);
-        const int64_t pair = u / p.n_rg;
         uint8_t* st = smem + (size_t)s * p.stage_bytes;
         if (lt < p.n_ct) {
           const int64_t t0 = (int64_t)lt * TILE;
@@ -289,8 +296,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
       const int issued = it;
       for (int j = issued - p.stages; j < issued; ++j) {
         if (j < 0) continue;
-        const int s = j % p.stages;
-        if (!mbar_wait_bounded(&full_bar[s], (j / p.stages) & 1, kWaitLimitNs)) {
+        const int s = j & (p.stages - 1);
+        if (!mbar_wait_bounded(&full_bar[s], (j >> p.stage_shift) & 1, kWaitLimitNs)) {
           atomicOr(p.err, 2);
           break;
         }
@@ -382,14 +389,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
       named_bar_sync(1, kConsumers);
     }
     // per-row constants of this unit
-    int tq_r[R];
-    bool rok[R];
+    uint32_t rok = 0;  // bit r: query row r of this unit exists
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int rr = rg * R + r;
-      rok[r] = rr < rows_valid;
-      tq_r[r] = rr % p.tq;
-    }
+    for (int r = 0; r < R; ++r)
+      if (rg * R + r < rows_valid) rok |= 1u << r;
 
     // ---------------------------------------------- this warp's slices of the unit
     float m_w[R], l_l[R];
@@ -403,8 +406,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
       const int it = static_cast<int>(t2 - t_begin);
       if (it % tgroups != wgroup) continue;
       const int lt = static_cast<int>(t2 - u * p.tpu);
-      const int s = it % p.stages;
-      if (!ms.abort && !mbar_wait_bounded(&full_bar[s], (it / p.stages) & 1, kWaitLimitNs)) {
+      const int s = it & (p.stages - 1);
+      if (!ms.abort && !mbar_wait_bounded(&full_bar[s], (it >> p.stage_shift) & 1, kWaitLimitNs)) {
         ms.abort = 1;
         atomicOr(p.err, 4);
       }
@@ -511,14 +514,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
       const int64_t tg1 = tg0 + 32;
 #pragma unroll
       for (int r = 0; r < R; ++r) {
-        bool ok0 = v0 && rok[r], ok1 = v1 && rok[r];
+        const bool rv = (rok >> r) & 1u;
+        bool ok0 = v0 && rv, ok1 = v1 && rv;
         if (per_token_mask) {
+          const int tqr = (rg * R + r) % p.tq;
           if (p.causal) {
-            ok0 = ok0 && tg0 <= q_off + tq_r[r];
-            ok1 = ok1 && tg1 <= q_off + tq_r[r];
+            ok0 = ok0 && tg0 <= q_off + tqr;
+            ok1 = ok1 && tg1 <= q_off + tqr;
           }
           if (p.mask) {
-            const float* mrow = p.mask + tq_r[r] * p.mask_stride;
+            const float* mrow = p.mask + tqr * p.mask_stride;
             if (ok0) {
               const float mv = mrow[tg0];
               if (p.mask_mode == 0) s0[r] += mv; else if (mv == 0.f) s0[r] = -FLT_MAX;
@@ -986,7 +991,8 @@ int run_decode(const ss_decode_args* a, float* part_out, void* stream) {
   p.k = a->k; p.nrep = a->hq / a->hkv; p.n_heavy = a->n_heavy;
   p.R = pl.R; p.tile = pl.tile; p.n_rg = pl.n_rg; p.n_ct = pl.n_ct; p.n_tt = pl.n_tt;
   p.tpu = pl.tpu; p.tc = a->tc; p.ttail = a->ttail; p.total_tiles = pl.total_tiles;
-  p.n_units = pl.n_units; p.grid = pl.grid; p.stages = pl.stages; p.max_cov = pl.max_cov;
+  p.n_units = pl.n_units; p.grid = pl.grid; p.stages = pl.stages;
+  p.stage_shift = pl.stages == 4 ? 2 : (pl.stages == 2 ? 1 : 0); p.max_cov = pl.max_cov;
   p.q = a->q; p.qdt = a->q_dtype; p.q_sb = a->q_sb; p.q_sh = a->q_sh; p.q_st = a->q_st;
   p.scale = a->scale;
   p.perm = a->perm; p.rot_k = a->rot_k; p.cents = a->centroids; p.heavy = a->heavy;
