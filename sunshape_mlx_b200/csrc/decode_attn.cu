@@ -324,6 +324,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
   const int mi = lane >> 3, mj = lane & 7;
   const int kk_off = (mi >= 2 ? 8 : 0) + mj;   // token row within a 16-token k-step
   const int dsel = mi & 1;                     // second 8-dim half of the 16-dim tile
+  // 128-byte-swizzle chunk offset of 16-dim MMA tile m (and m + 4 in the next box)
+  uint32_t swz[4];
+#pragma unroll
+  for (int m = 0; m < 4; ++m) swz[m] = static_cast<uint32_t>(((2 * m + dsel) ^ mj) << 4);
   const int rows_valid = p.nrep * p.tq;
   const bool per_token_mask = p.causal || p.mask != nullptr;
   // columns R..7 of every P slice stay zero
@@ -402,10 +406,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
 
-    for (int64_t t2 = tau; t2 < u_end; ++t2) {
-      const int it = static_cast<int>(t2 - t_begin);
-      if (it % tgroups != wgroup) continue;
-      const int lt = static_cast<int>(t2 - u * p.tpu);
+    // this warp's tiles of the unit: it = tau - t_begin + i with it % tgroups == wgroup
+    const int it0 = static_cast<int>(tau - t_begin);
+    const int lt0 = static_cast<int>(tau - u * p.tpu);
+    const int n_here = static_cast<int>(u_end - tau);
+    const int ifirst = (wgroup - it0 % tgroups + tgroups) % tgroups;
+    for (int i = ifirst; i < n_here; i += tgroups) {
+      const int it = it0 + i;
+      const int lt = lt0 + i;
       const int s = it & (p.stages - 1);
       if (!ms.abort && !mbar_wait_bounded(&full_bar[s], (it >> p.stage_shift) & 1, kWaitLimitNs)) {
         ms.abort = 1;
@@ -414,9 +422,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
       const bool aborted = ms.abort != 0;
       uint8_t* st = smem + (size_t)s * p.stage_bytes;
       const bool compressed = lt < p.n_ct;
-      const int64_t t0 = compressed ? (int64_t)lt * TILE : (int64_t)(lt - p.n_ct) * TILE;
-      const int64_t rem_ = (compressed ? p.tc : p.ttail) - t0;
-      const int len = static_cast<int>(rem_ < TILE ? rem_ : TILE);
+      const int t0 = (compressed ? lt : lt - p.n_ct) * TILE;
+      const int rem_ = static_cast<int>(compressed ? p.tc : p.ttail) - t0;
+      const int len = rem_ < TILE ? rem_ : TILE;
       const int tok0 = slice * SL + lane;       // tokens of this lane within the tile
       const int tok1 = TPL > 1 ? tok0 + 32 : tok0;
       const bool v0 = tok0 < len && !aborted, v1 = TPL > 1 && tok1 < len && !aborted;
@@ -430,7 +438,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
         const uint8_t* ir1 = st + p.off_idx + tok1 * p.nb;
         if (NBC > 0 || (p.nb & 3) == 0) {
           const int nbw = NBC > 0 ? NBC / 4 : (p.nb >> 2);
-          const uint32_t kstride = static_cast<uint32_t>(p.k) * R;  // floats per block
+          // floats per block of the table (compile-time for 16 blocks x 256 centroids)
+          const uint32_t kstride = NBC > 0 ? 256u * R : static_cast<uint32_t>(p.k) * R;
 #pragma unroll
           for (int w = 0; w < (NBC > 0 ? NBC / 4 : 32); ++w) {
             if (NBC == 0 && w >= nbw) break;
@@ -439,8 +448,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               const uint32_t bo = (4 * w + j) * kstride;
-              const float* e0 = lut + (bo + ((c0w >> (8 * j)) & 0xffu) * R);
-              const float* e1 = lut + (bo + ((c1w >> (8 * j)) & 0xffu) * R);
+              const float* e0 = lut + bo + __byte_perm(c0w, 0u, 0x4440u + j) * R;
+              const float* e1 = lut + bo + __byte_perm(c1w, 0u, 0x4440u + j) * R;
               if constexpr (R % 4 == 0) {
 #pragma unroll
                 for (int r4 = 0; r4 < R; r4 += 4) {
@@ -510,8 +519,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
         }
       }
       // masking: invalid tokens / rows -> -inf; causal; mask arrays
-      const int64_t tg0 = (compressed ? t0 : p.tc + t0) + tok0;
-      const int64_t tg1 = tg0 + 32;
+      const int tg0 = (compressed ? t0 : static_cast<int>(p.tc) + t0) + tok0;
+      const int tg1 = tg0 + 32;
 #pragma unroll
       for (int r = 0; r < R; ++r) {
         const bool rv = (rok >> r) & 1u;
@@ -584,7 +593,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
           ldsm_x2_trans(pw_addr + ks * 256, b0, b1);
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt) {
-            const uint32_t col = (mt >> 2) * (TILE * 128) + ((((2 * mt + dsel) & 7) ^ mj) << 4);
+            const uint32_t col = (mt >> 2) * (TILE * 128) + swz[mt & 3];
             uint32_t x0, x1, x2, x3;
             ldsm_x4_trans(vb + ks * 2048 + col, x0, x1, x2, x3);
             mma_16816(acc[mt], x0, x1, x2, x3, b0, b1);
@@ -919,7 +928,8 @@ int make_plan(const ss_decode_args* a, Plan& pl) {
 template <int R, int D>
 int launch_decode(const DecodeParams& p, const CUtensorMap& mv, const CUtensorMap& mvt,
                   size_t smem, cudaStream_t st) {
-  auto kern = p.nb == 16 ? decode_attn_kernel<R, D, 16> : decode_attn_kernel<R, D, 0>;
+  auto kern = (p.nb == 16 && p.k == 256) ? decode_attn_kernel<R, D, 16>
+                                         : decode_attn_kernel<R, D, 0>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess)
