@@ -137,6 +137,11 @@ __device__ __forceinline__ void tma_load_3d(void* dst_smem, const CUtensorMap* m
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
       : "memory");
 }
+// Orders this thread's earlier generic-proxy shared-memory accesses before
+// subsequent async-proxy (bulk copy) writes to the same memory.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

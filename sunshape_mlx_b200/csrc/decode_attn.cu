@@ -91,6 +91,8 @@ struct DecodeParams {
   int* err;
   int* counters;
   float* slots;
+  float* lut_g;             // per-unit query x centroid tables [unit][nb][k][R]
+  uint32_t lut_unit_bytes;
   // shared-memory carve-up (bytes from the 1024-aligned base)
   uint32_t off_stage, stage_bytes, off_idx, off_aux, off_vdq, off_lut, off_p, off_misc;
 };
@@ -133,49 +135,91 @@ struct Misc {  // small shared-memory state
   int abort;
 };
 
-// Query x centroid table of one unit: lut[b][c][r] = <qc_r,b , C[b][c]>.
-// Thread t owns block b = t % nb (its R query sub-vectors stay in registers)
-// and centroids c = t / nb + i * (256 / nb); centroid rows are read as
-// 16-byte vectors. Heavy blocks scored from their fp16 values get zeros.
-template <int R, int BD>
-__device__ __forceinline__ void build_lut(const DecodeParams& p, const Misc& ms, float* lut,
-                                          int ctid) {
-  const int nb = p.nb;
-  const int b = ctid % nb;
-  const int c0 = ctid / nb, cstep = kConsumers / nb;
-  const bool zero = p.n_heavy > 0 && ms.is_heavy[b];
-  float q[R][BD];
-#pragma unroll
-  for (int r = 0; r < R; ++r)
-#pragma unroll
-    for (int j = 0; j < BD; ++j) q[r][j] = ms.qc[r][b * BD + j];
-  const float* cb = p.cents + (size_t)b * p.k * BD;
-  float* lb = lut + (size_t)b * p.k * R;
-#pragma unroll 4
-  for (int c = c0; c < p.k; c += cstep) {
-    float cv[BD];
-#pragma unroll
-    for (int j = 0; j < BD; j += 4) {
-      const float4 v = __ldg(reinterpret_cast<const float4*>(cb + (size_t)c * BD + j));
-      cv[j] = v.x; cv[j + 1] = v.y; cv[j + 2] = v.z; cv[j + 3] = v.w;
+// Scaled query rows of a unit in the original basis: qo[r] = dtype(q * scale)
+// (attention.py:208) for row r = (GQA repeat, query token) of group rg.
+__device__ __forceinline__ void unit_query_rows(const DecodeParams& p, Misc& ms, int rg, int bb,
+                                                int hh, int tid, int nthr) {
+  const float sc = round_to(p.scale, p.qdt);
+  const int rows_valid = p.nrep * p.tq;
+  for (int e = tid; e < p.R * p.d; e += nthr) {
+    const int r = e / p.d, j = e - r * p.d;
+    const int rr = rg * p.R + r;
+    float v = 0.f;
+    if (rr < rows_valid) {
+      const int rep = rr / p.tq, tqi = rr - rep * p.tq;
+      const int qh = hh * p.nrep + rep;
+      const float x = load_as_f32(p.q, p.qdt, bb * p.q_sb + qh * p.q_sh + tqi * p.q_st + j);
+      v = round_to(x * sc, p.qdt);
     }
+    ms.qo[r][j] = v;
+  }
+}
+
+// The same rows in codec space: permutation (ProfilePerm) or rotation.
+__device__ __forceinline__ void unit_codec_rows(const DecodeParams& p, Misc& ms, int tid, int nthr) {
+  for (int e = tid; e < p.R * p.d; e += nthr) {
+    const int r = e / p.d, j = e - r * p.d;
+    float v;
+    if (p.rot_k) {
+      float a = 0.f;
+      for (int i = 0; i < p.d; ++i) a = fmaf(ms.qo[r][i], p.rot_k[j * p.d + i], a);
+      v = a;
+    } else {
+      v = ms.qo[r][p.perm ? p.perm[j] : j];
+    }
+    ms.qc[r][j] = v;
+  }
+}
+
+// Grid (units, block chunks): CTA (u, g) computes table rows of blocks
+// [g * kLutBlocks, (g + 1) * kLutBlocks) of unit u into the workspace, laid
+// out [unit][nb][k][R]; one thread per (block, centroid), R rows each.
+constexpr int kLutBlocks = 4;
+template <int R>
+__global__ void __launch_bounds__(kConsumers) lut_kernel(const __grid_constant__ DecodeParams p) {
+  __shared__ Misc ms;
+  const int tid = threadIdx.x;
+  const int64_t u = blockIdx.x;
+  const int b0 = blockIdx.y * kLutBlocks;
+  const int64_t pair = u / p.n_rg;
+  const int rg = static_cast<int>(u - pair * p.n_rg);
+  const int bb = static_cast<int>(pair / p.hkv), hh = static_cast<int>(pair % p.hkv);
+  unit_query_rows(p, ms, rg, bb, hh, tid, kConsumers);
+  __syncthreads();
+  unit_codec_rows(p, ms, tid, kConsumers);
+  __syncthreads();
+  float* out = p.lut_g + (size_t)u * (p.lut_unit_bytes / 4);
+  const int nbl = min(kLutBlocks, p.nb - b0);
+  for (int e = tid; e < nbl * p.k; e += kConsumers) {
+    const int b = b0 + e / p.k, c = e % p.k;
+    const bool zero = p.n_heavy > 0 && p.heavy && p.heavy[b];
+    const float* cv = p.cents + ((size_t)b * p.k + c) * p.bd;
+    const float* qb = &ms.qc[0][b * p.bd];
     float o[R];
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      float a = 0.f;
+    for (int r = 0; r < R; ++r) o[r] = 0.f;
+    if (p.bd % 4 == 0) {
+      for (int j = 0; j < p.bd; j += 4) {
+        const float4 c4 = __ldg(reinterpret_cast<const float4*>(cv + j));
 #pragma unroll
-      for (int j = 0; j < BD; ++j) a = fmaf(q[r][j], cv[j], a);
-      o[r] = zero ? 0.f : a;
-    }
-    float* dst = lb + (size_t)c * R;
-    if constexpr (R % 4 == 0) {
-#pragma unroll
-      for (int r = 0; r < R; r += 4)
-        *reinterpret_cast<float4*>(dst + r) = make_float4(o[r], o[r + 1], o[r + 2], o[r + 3]);
+        for (int r = 0; r < R; ++r) {
+          const float* q = qb + r * 128 + j;
+          o[r] = fmaf(q[0], c4.x, o[r]);
+          o[r] = fmaf(q[1], c4.y, o[r]);
+          o[r] = fmaf(q[2], c4.z, o[r]);
+          o[r] = fmaf(q[3], c4.w, o[r]);
+        }
+      }
     } else {
+      for (int j = 0; j < p.bd; ++j) {
+        const float cj = __ldg(cv + j);
 #pragma unroll
-      for (int r = 0; r < R; ++r) dst[r] = o[r];
+        for (int r = 0; r < R; ++r) o[r] = fmaf(qb[r * 128 + j], cj, o[r]);
+      }
     }
+    float* dst = out + ((size_t)b * p.k + c) * R;
+#pragma unroll
+    for (int r = 0; r < R; ++r) dst[r] = zero ? 0.f : o[r];
   }
 }
 
@@ -187,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
   // Align to 1024 B (128-byte-swizzle atoms) by an offset from the __shared__
   // array itself, so every access below stays a shared-memory access.
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  __shared__ uint64_t full_bar[kMaxStages], empty_bar[kMaxStages];
+  __shared__ uint64_t full_bar[kMaxStages], empty_bar[kMaxStages], lut_bar;
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -204,6 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], TILE / slice_tokens(R));
     }
+    mbar_init(&lut_bar, 1);
     ms.abort = 0;
     int hp = 0;
     for (int b = 0; b < p.nb; ++b) {
@@ -335,6 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
     if ((e & 7) >= R) Pw[e] = __float2half_rn(0.f);
 
   int64_t tau = t_begin;
+  uint32_t unit_no = 0;
   while (tau < t_end) {
     const int64_t u = tau / p.tpu;
     const int64_t u_end = min(t_end, (u + 1) * p.tpu);
@@ -342,57 +388,31 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
     const int rg = static_cast<int>(u - pair * p.n_rg);
     const int bb = static_cast<int>(pair / p.hkv), hh = static_cast<int>(pair % p.hkv);
 
-    // ---------------------------------------------- build the unit's LUT
+    // ---------------------------------------------- the unit's LUT
+    // Tables are precomputed for all units by lut_kernel; one bulk copy brings
+    // this unit's table into shared memory. Query rows are only needed here
+    // for exact dot products (fp16 tail tokens, heavy blocks).
     named_bar_sync(1, kConsumers);  // previous unit finalised, LUT region free
-    {
-      const float sc = round_to(p.scale, p.qdt);
-      for (int e = ctid; e < R * p.d; e += kConsumers) {
-        const int r = e / p.d, j = e - r * p.d;
-        const int rr = rg * R + r;
-        float v = 0.f;
-        if (rr < rows_valid) {
-          const int rep = rr / p.tq, tqi = rr - rep * p.tq;
-          const int qh = hh * p.nrep + rep;
-          const float x = load_as_f32(p.q, p.qdt, bb * p.q_sb + qh * p.q_sh + tqi * p.q_st + j);
-          v = round_to(x * sc, p.qdt);
-        }
-        ms.qo[r][j] = v;
-      }
+    if (ctid == 0) {
+      fence_proxy_async_smem();  // region was last written as merge scratch
+      const uint32_t bytes = p.lut_unit_bytes;
+      mbar_arrive_expect_tx(&lut_bar, bytes);
+      const uint8_t* src = reinterpret_cast<const uint8_t*>(p.lut_g) + (size_t)u * bytes;
+      for (uint32_t off = 0; off < bytes; off += 16384u)
+        bulk_g2s(reinterpret_cast<uint8_t*>(lut) + off, src + off,
+                 bytes - off < 16384u ? bytes - off : 16384u, &lut_bar);
+    }
+    if (p.ttail > 0 || p.n_heavy > 0) {
+      unit_query_rows(p, ms, rg, bb, hh, ctid, kConsumers);
       named_bar_sync(1, kConsumers);
-      for (int e = ctid; e < R * p.d; e += kConsumers) {
-        const int r = e / p.d, j = e - r * p.d;
-        float v;
-        if (p.rot_k) {
-          float a = 0.f;
-          for (int i = 0; i < p.d; ++i) a = fmaf(ms.qo[r][i], p.rot_k[j * p.d + i], a);
-          v = a;
-        } else {
-          v = ms.qo[r][p.perm ? p.perm[j] : j];
-        }
-        ms.qc[r][j] = v;
-      }
-      named_bar_sync(1, kConsumers);
-      if (p.bd == 8 && kConsumers % p.nb == 0) {
-        build_lut<R, 8>(p, ms, lut, ctid);
-      } else if (p.bd == 4 && kConsumers % p.nb == 0) {
-        build_lut<R, 4>(p, ms, lut, ctid);
-      } else {
-        for (int e = ctid; e < p.nb * p.k; e += kConsumers) {
-          const int b = e / p.k;
-          const float* c = p.cents + (size_t)e * p.bd;
-          const bool zero = p.n_heavy > 0 && ms.is_heavy[b];
-          float* dst = lut + (size_t)e * R;
-#pragma unroll
-          for (int r = 0; r < R; ++r) {
-            float a = 0.f;
-            for (int j = 0; j < p.bd; ++j) a = fmaf(ms.qc[r][b * p.bd + j], __ldg(c + j), a);
-            dst[r] = zero ? 0.f : a;
-          }
-        }
-      }
+      unit_codec_rows(p, ms, ctid, kConsumers);
       named_bar_sync(1, kConsumers);
     }
-    // per-row constants of this unit
+    if (!ms.abort && !mbar_wait_bounded(&lut_bar, unit_no & 1, kWaitLimitNs)) {
+      ms.abort = 1;
+      atomicOr(p.err, 8);
+    }
+    ++unit_no;
     uint32_t rok = 0;  // bit r: query row r of this unit exists
 #pragma unroll
     for (int r = 0; r < R; ++r)
@@ -827,7 +847,7 @@ struct Plan {
   int64_t total_tiles, n_units;
   uint32_t stage_bytes, off_idx, off_aux, off_vdq, off_lut, off_p, off_misc;
   size_t smem;
-  size_t ws_bytes, off_counters, off_slots;
+  size_t ws_bytes, off_counters, off_slots, off_lut_g, lut_unit_bytes;
 };
 
 constexpr size_t kSmemBudget = 226 * 1024;  // leaves room for static barriers
@@ -921,13 +941,20 @@ int make_plan(const ss_decode_args* a, Plan& pl) {
   // workspace: [error word | counters | partial slots]
   pl.off_counters = 256;
   pl.off_slots = (pl.off_counters + (size_t)pl.n_units * 4 + 255) & ~size_t(255);
-  pl.ws_bytes = pl.off_slots + (size_t)pl.n_units * pl.max_cov * R * (a->d + 2) * 4;
+  pl.lut_unit_bytes = (size_t)nb * a->k * R * 4;
+  pl.off_lut_g = (pl.off_slots + (size_t)pl.n_units * pl.max_cov * R * (a->d + 2) * 4 + 255) &
+                 ~size_t(255);
+  pl.ws_bytes = pl.off_lut_g + (size_t)pl.n_units * pl.lut_unit_bytes;
   return SS_OK;
 }
 
 template <int R, int D>
 int launch_decode(const DecodeParams& p, const CUtensorMap& mv, const CUtensorMap& mvt,
                   size_t smem, cudaStream_t st) {
+  lut_kernel<R><<<dim3(static_cast<unsigned>(p.n_units), (p.nb + kLutBlocks - 1) / kLutBlocks),
+                  kConsumers, 0, st>>>(p);
+  int rc = check_launch("ss_decode_attn (tables)");
+  if (rc != SS_OK) return rc;
   auto kern = (p.nb == 16 && p.k == 256) ? decode_attn_kernel<R, D, 16>
                                          : decode_attn_kernel<R, D, 0>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1023,6 +1050,8 @@ int run_decode(const ss_decode_args* a, float* part_out, void* stream) {
   p.err = reinterpret_cast<int*>(ws);
   p.counters = reinterpret_cast<int*>(ws + pl.off_counters);
   p.slots = reinterpret_cast<float*>(ws + pl.off_slots);
+  p.lut_g = reinterpret_cast<float*>(ws + pl.off_lut_g);
+  p.lut_unit_bytes = static_cast<uint32_t>(pl.lut_unit_bytes);
   p.stage_bytes = pl.stage_bytes; p.off_idx = pl.off_idx; p.off_aux = pl.off_aux;
   p.off_vdq = pl.off_vdq; p.off_lut = pl.off_lut; p.off_p = pl.off_p; p.off_misc = pl.off_misc;
   p.off_stage = 0;
