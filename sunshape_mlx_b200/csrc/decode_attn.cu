@@ -171,11 +171,14 @@ __device__ __forceinline__ void unit_codec_rows(const DecodeParams& p, Misc& ms,
   }
 }
 
-// Grid (units, block chunks): CTA (u, g) computes table rows of blocks
+// Grid (units, block chunks): CTA (u, g) computes the table of blocks
 // [g * kLutBlocks, (g + 1) * kLutBlocks) of unit u into the workspace, laid
-// out [unit][nb][k][R]; one thread per (block, centroid), R rows each.
+// out [unit][nb][k][R]. Thread t owns block b0 + t / 64 (its R query
+// sub-vectors in registers) and centroids t % 64 + i * 64, so a warp writes
+// contiguous table rows.
+// BD = 0 is the generic path for block sizes other than 4 and 8.
 constexpr int kLutBlocks = 4;
-template <int R>
+template <int R, int BD>
 __global__ void __launch_bounds__(kConsumers) lut_kernel(const __grid_constant__ DecodeParams p) {
   __shared__ Misc ms;
   const int tid = threadIdx.x;
@@ -189,37 +192,57 @@ __global__ void __launch_bounds__(kConsumers) lut_kernel(const __grid_constant__
   unit_codec_rows(p, ms, tid, kConsumers);
   __syncthreads();
   float* out = p.lut_g + (size_t)u * (p.lut_unit_bytes / 4);
-  const int nbl = min(kLutBlocks, p.nb - b0);
-  for (int e = tid; e < nbl * p.k; e += kConsumers) {
-    const int b = b0 + e / p.k, c = e % p.k;
+  if constexpr (BD > 0) {
+    const int b = b0 + tid / (kConsumers / kLutBlocks);
+    if (b >= p.nb) return;
     const bool zero = p.n_heavy > 0 && p.heavy && p.heavy[b];
-    const float* cv = p.cents + ((size_t)b * p.k + c) * p.bd;
-    const float* qb = &ms.qc[0][b * p.bd];
-    float o[R];
+    float q[R][BD];
 #pragma unroll
-    for (int r = 0; r < R; ++r) o[r] = 0.f;
-    if (p.bd % 4 == 0) {
-      for (int j = 0; j < p.bd; j += 4) {
-        const float4 c4 = __ldg(reinterpret_cast<const float4*>(cv + j));
+    for (int r = 0; r < R; ++r)
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
-          const float* q = qb + r * 128 + j;
-          o[r] = fmaf(q[0], c4.x, o[r]);
-          o[r] = fmaf(q[1], c4.y, o[r]);
-          o[r] = fmaf(q[2], c4.z, o[r]);
-          o[r] = fmaf(q[3], c4.w, o[r]);
-        }
+      for (int j = 0; j < BD; ++j) q[r][j] = zero ? 0.f : ms.qc[r][b * BD + j];
+    const float* cb = p.cents + (size_t)b * p.k * BD;
+    float* ob = out + (size_t)b * p.k * R;
+#pragma unroll 4
+    for (int c = tid % (kConsumers / kLutBlocks); c < p.k; c += kConsumers / kLutBlocks) {
+      float cv[BD];
+#pragma unroll
+      for (int j = 0; j < BD; j += 4) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(cb + (size_t)c * BD + j));
+        cv[j] = v.x; cv[j + 1] = v.y; cv[j + 2] = v.z; cv[j + 3] = v.w;
       }
-    } else {
-      for (int j = 0; j < p.bd; ++j) {
-        const float cj = __ldg(cv + j);
+      float o[R];
 #pragma unroll
-        for (int r = 0; r < R; ++r) o[r] = fmaf(qb[r * 128 + j], cj, o[r]);
+      for (int r = 0; r < R; ++r) {
+        float acc = 0.f;
+#pragma unroll
+        for (int j = 0; j < BD; ++j) acc = fmaf(q[r][j], cv[j], acc);
+        o[r] = acc;
+      }
+      float* dst = ob + (size_t)c * R;
+      if constexpr (R % 4 == 0) {
+#pragma unroll
+        for (int r = 0; r < R; r += 4)
+          *reinterpret_cast<float4*>(dst + r) = make_float4(o[r], o[r + 1], o[r + 2], o[r + 3]);
+      } else {
+#pragma unroll
+        for (int r = 0; r < R; ++r) dst[r] = o[r];
       }
     }
-    float* dst = out + ((size_t)b * p.k + c) * R;
+  } else {
+    const int nbl = min(kLutBlocks, p.nb - b0);
+    for (int e = tid; e < nbl * p.k; e += kConsumers) {
+      const int b = b0 + e / p.k, c = e % p.k;
+      const bool zero = p.n_heavy > 0 && p.heavy && p.heavy[b];
+      const float* cv = p.cents + ((size_t)b * p.k + c) * p.bd;
+      float* dst = out + ((size_t)b * p.k + c) * R;
 #pragma unroll
-    for (int r = 0; r < R; ++r) dst[r] = zero ? 0.f : o[r];
+      for (int r = 0; r < R; ++r) {
+        float acc = 0.f;
+        for (int j = 0; j < p.bd; ++j) acc = fmaf(ms.qc[r][b * p.bd + j], __ldg(cv + j), acc);
+        dst[r] = zero ? 0.f : acc;
+      }
+    }
   }
 }
 
@@ -951,8 +974,19 @@ int make_plan(const ss_decode_args* a, Plan& pl) {
 template <int R, int D>
 int launch_decode(const DecodeParams& p, const CUtensorMap& mv, const CUtensorMap& mvt,
                   size_t smem, cudaStream_t st) {
-  lut_kernel<R><<<dim3(static_cast<unsigned>(p.n_units), (p.nb + kLutBlocks - 1) / kLutBlocks),
-                  kConsumers, 0, st>>>(p);
+  const dim3 lgrid(static_cast<unsigned>(p.n_units), (p.nb + kLutBlocks - 1) / kLutBlocks);
+  // Same shared-memory carveout as the decode kernel: no reconfiguration
+  // between the two launches of every step.
+  static bool carveout_set = false;
+  if (!carveout_set) {
+    cudaFuncSetAttribute(lut_kernel<R, 8>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    cudaFuncSetAttribute(lut_kernel<R, 4>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    cudaFuncSetAttribute(lut_kernel<R, 0>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    carveout_set = true;
+  }
+  if (p.bd == 8) lut_kernel<R, 8><<<lgrid, kConsumers, 0, st>>>(p);
+  else if (p.bd == 4) lut_kernel<R, 4><<<lgrid, kConsumers, 0, st>>>(p);
+  else lut_kernel<R, 0><<<lgrid, kConsumers, 0, st>>>(p);
   int rc = check_launch("ss_decode_attn (tables)");
   if (rc != SS_OK) return rc;
   auto kern = (p.nb == 16 && p.k == 256) ? decode_attn_kernel<R, D, 16>
