@@ -137,6 +137,15 @@ __device__ __forceinline__ void tma_load_3d(void* dst_smem, const CUtensorMap* m
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
       : "memory");
 }
+// Programmatic dependent launch: the primary grid allows its dependent to be
+// scheduled; the dependent waits for the primary's completion and memory.
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // Orders this thread's earlier generic-proxy shared-memory accesses before
 // subsequent async-proxy (bulk copy) writes to the same memory.
 __device__ __forceinline__ void fence_proxy_async_smem() {

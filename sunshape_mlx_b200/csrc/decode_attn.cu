@@ -187,6 +187,7 @@ __global__ void __launch_bounds__(kConsumers) lut_kernel(const __grid_constant__
   const int64_t pair = u / p.n_rg;
   const int rg = static_cast<int>(u - pair * p.n_rg);
   const int bb = static_cast<int>(pair / p.hkv), hh = static_cast<int>(pair % p.hkv);
+  grid_launch_dependents();  // let the decode grid start streaming now
   unit_query_rows(p, ms, rg, bb, hh, tid, kConsumers);
   __syncthreads();
   unit_codec_rows(p, ms, tid, kConsumers);
@@ -417,6 +418,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
     // for exact dot products (fp16 tail tokens, heavy blocks).
     named_bar_sync(1, kConsumers);  // previous unit finalised, LUT region free
     if (ctid == 0) {
+      // Tables come from lut_kernel, launched just before as the primary of a
+      // programmatic dependent launch: wait for its results once.
+      if (unit_no == 0) grid_dependency_wait();
       fence_proxy_async_smem();  // region was last written as merge scratch
       const uint32_t bytes = p.lut_unit_bytes;
       mbar_arrive_expect_tx(&lut_bar, bytes);
@@ -995,7 +999,19 @@ int launch_decode(const DecodeParams& p, const CUtensorMap& mv, const CUtensorMa
                                        static_cast<int>(smem));
   if (e != cudaSuccess)
     return fail(SS_ERR_CUDA, std::string("ss_decode_attn: smem attribute: ") + cudaGetErrorString(e));
-  kern<<<p.grid, kThreads, smem, st>>>(p, mv, mvt);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, p, mv, mvt);
+  if (e != cudaSuccess)
+    return fail(SS_ERR_CUDA, std::string("ss_decode_attn: launch: ") + cudaGetErrorString(e));
   return check_launch("ss_decode_attn");
 }
 
