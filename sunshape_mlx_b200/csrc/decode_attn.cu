@@ -137,8 +137,8 @@ struct Misc {  // small shared-memory state
 
 // Scaled query rows of a unit in the original basis: qo[r] = dtype(q * scale)
 // (attention.py:208) for row r = (GQA repeat, query token) of group rg.
-__device__ __forceinline__ void unit_query_rows(const DecodeParams& p, Misc& ms, int rg, int bb,
-                                                int hh, int tid, int nthr) {
+__device__ __forceinline__ void unit_query_rows(const DecodeParams& p, float (*qo)[128], int rg,
+                                                int bb, int hh, int tid, int nthr) {
   const float sc = round_to(p.scale, p.qdt);
   const int rows_valid = p.nrep * p.tq;
   for (int e = tid; e < p.R * p.d; e += nthr) {
@@ -151,23 +151,24 @@ __device__ __forceinline__ void unit_query_rows(const DecodeParams& p, Misc& ms,
       const float x = load_as_f32(p.q, p.qdt, bb * p.q_sb + qh * p.q_sh + tqi * p.q_st + j);
       v = round_to(x * sc, p.qdt);
     }
-    ms.qo[r][j] = v;
+    qo[r][j] = v;
   }
 }
 
 // The same rows in codec space: permutation (ProfilePerm) or rotation.
-__device__ __forceinline__ void unit_codec_rows(const DecodeParams& p, Misc& ms, int tid, int nthr) {
+__device__ __forceinline__ void unit_codec_rows(const DecodeParams& p, const float (*qo)[128],
+                                                float (*qc)[128], int tid, int nthr) {
   for (int e = tid; e < p.R * p.d; e += nthr) {
     const int r = e / p.d, j = e - r * p.d;
     float v;
     if (p.rot_k) {
       float a = 0.f;
-      for (int i = 0; i < p.d; ++i) a = fmaf(ms.qo[r][i], p.rot_k[j * p.d + i], a);
+      for (int i = 0; i < p.d; ++i) a = fmaf(qo[r][i], p.rot_k[j * p.d + i], a);
       v = a;
     } else {
-      v = ms.qo[r][p.perm ? p.perm[j] : j];
+      v = qo[r][p.perm ? p.perm[j] : j];
     }
-    ms.qc[r][j] = v;
+    qc[r][j] = v;
   }
 }
 
@@ -180,7 +181,9 @@ __device__ __forceinline__ void unit_codec_rows(const DecodeParams& p, Misc& ms,
 constexpr int kLutBlocks = 4;
 template <int R, int BD>
 __global__ void __launch_bounds__(kConsumers) lut_kernel(const __grid_constant__ DecodeParams p) {
-  __shared__ Misc ms;
+  // only this unit's R query rows (keeps the CTA small enough to share an SM
+  // with a decode CTA)
+  __shared__ float qo[R][128], qc[R][128];
   const int tid = threadIdx.x;
   const int64_t u = blockIdx.x;
   const int b0 = blockIdx.y * kLutBlocks;
@@ -188,9 +191,9 @@ __global__ void __launch_bounds__(kConsumers) lut_kernel(const __grid_constant__
   const int rg = static_cast<int>(u - pair * p.n_rg);
   const int bb = static_cast<int>(pair / p.hkv), hh = static_cast<int>(pair % p.hkv);
   grid_launch_dependents();  // let the decode grid start streaming now
-  unit_query_rows(p, ms, rg, bb, hh, tid, kConsumers);
+  unit_query_rows(p, qo, rg, bb, hh, tid, kConsumers);
   __syncthreads();
-  unit_codec_rows(p, ms, tid, kConsumers);
+  unit_codec_rows(p, qo, qc, tid, kConsumers);
   __syncthreads();
   float* out = p.lut_g + (size_t)u * (p.lut_unit_bytes / 4);
   if constexpr (BD > 0) {
@@ -201,7 +204,7 @@ __global__ void __launch_bounds__(kConsumers) lut_kernel(const __grid_constant__
 #pragma unroll
     for (int r = 0; r < R; ++r)
 #pragma unroll
-      for (int j = 0; j < BD; ++j) q[r][j] = zero ? 0.f : ms.qc[r][b * BD + j];
+      for (int j = 0; j < BD; ++j) q[r][j] = zero ? 0.f : qc[r][b * BD + j];
     const float* cb = p.cents + (size_t)b * p.k * BD;
     float* ob = out + (size_t)b * p.k * R;
 #pragma unroll 4
@@ -240,7 +243,7 @@ __global__ void __launch_bounds__(kConsumers) lut_kernel(const __grid_constant__
 #pragma unroll
       for (int r = 0; r < R; ++r) {
         float acc = 0.f;
-        for (int j = 0; j < p.bd; ++j) acc = fmaf(ms.qc[r][b * p.bd + j], __ldg(cv + j), acc);
+        for (int j = 0; j < p.bd; ++j) acc = fmaf(qc[r][b * p.bd + j], __ldg(cv + j), acc);
         dst[r] = zero ? 0.f : acc;
       }
     }
@@ -430,9 +433,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
                  bytes - off < 16384u ? bytes - off : 16384u, &lut_bar);
     }
     if (p.ttail > 0 || p.n_heavy > 0) {
-      unit_query_rows(p, ms, rg, bb, hh, ctid, kConsumers);
+      unit_query_rows(p, ms.qo, rg, bb, hh, ctid, kConsumers);
       named_bar_sync(1, kConsumers);
-      unit_codec_rows(p, ms, ctid, kConsumers);
+      unit_codec_rows(p, ms.qo, ms.qc, ctid, kConsumers);
       named_bar_sync(1, kConsumers);
     }
     if (!ms.abort && !mbar_wait_bounded(&lut_bar, unit_no & 1, kWaitLimitNs)) {
