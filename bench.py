@@ -269,7 +269,7 @@ def run_ours(args, world, rank, local):
         e2e = {"value": world * B * HQ / (ems / 1e3), "unit": "queries/s",
                "h2d_bytes_per_step": qh.numel() * 2 + kh.numel() * 2 + vh.numel() * 2,
                "d2h_bytes_per_step": oh.numel() * 2, "ms_per_step": ems,
-               "gpu_launches_per_step": 2}
+               "gpu_launches_per_step": 3}  # assign (append) + table + decode
 
     if rank != 0:
         return None
@@ -288,7 +288,7 @@ def run_ours(args, world, rank, local):
                      "frac": achieved / peak, "peak_source": peak_kind,
                      "frac_of_8TBs_nominal": achieved / 8000.0,
                      "traffic": _traffic(), "algorithmic_bytes_per_launch": alg_bytes},
-        "gpu_launches": args.steps,
+        "gpu_launches": 2 * args.steps,  # table kernel + decode kernel per step
         "clocks": clocks,
         "e2e": e2e,
     }
