@@ -83,6 +83,19 @@ int ss_vq_assign(const void* keys, int key_dtype, int64_t n_groups, int64_t rows
                  int64_t idx_row_stride, uint16_t* out_heavy, int64_t heavy_group_stride,
                  int64_t heavy_row_stride, float* out_pt, int dist_mode, void* stream);
 
+/* Assignment kernel selection (no counterpart in the reference, which has one
+ * CPU loop and one Metal kernel): 0 = automatic (tensor-core kernel for
+ * >= 512 rows when bd in {4,8,16}, k % 32 == 0, d <= 128 and key rows are
+ * 16-byte aligned; CUDA-core kernel otherwise), 1 = CUDA-core kernel only,
+ * 2 = tensor-core kernel or SS_ERR_UNSUPPORTED. Process-wide. Both kernels
+ * return the same indices. */
+int ss_set_assign_path(int path);
+
+/* Synchronizes the stream, then reads and clears the tensor-core assignment
+ * kernel's sticky status: SS_ERR_TIMEOUT if one of its pipeline waits gave
+ * up (2 s bound; indices of that launch are then invalid), else SS_OK. */
+int ss_vq_assign_check(void* stream);
+
 /* k-means update over one assignment (codec.py:93-101): for every block b and
  * centroid c the float32 sum of the assigned rows, accumulated in row order
  * (np.add.at), divided by the count in float64; empty clusters keep their

@@ -98,6 +98,8 @@ _SIGS = {
     "ss_decode_attn": ([C.POINTER(DecodeArgs), vp], i32),
     "ss_decode_attn_partial": ([C.POINTER(DecodeArgs), vp, vp], i32),
     "ss_decode_check": ([vp, vp], i32),
+    "ss_set_assign_path": ([i32], i32),
+    "ss_vq_assign_check": ([vp], i32),
     "ss_decode_attn_noalloc": ([C.POINTER(DecodeArgs), vp], i32),
     "ss_lse_merge": ([vp, i32, i64, i32, vp, vp, i32, i64, vp], i32),
 }

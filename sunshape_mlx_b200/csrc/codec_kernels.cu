@@ -8,48 +8,13 @@
 // (6+7))). All float ops use explicit round-to-nearest intrinsics so the
 // compiler cannot contract them into FMAs.
 #include "common.cuh"
+#include "vq_math.cuh"
 
 namespace ss {
 namespace {
 
 constexpr int kAssignThreads = 512;
 constexpr int kAssignRows = 32;  // rows per tile (one per lane)
-
-// NumPy pairwise sum of n <= 16 float32 terms (numpy/_core/src/umath/loops_utils.h).
-template <int N>
-__device__ __forceinline__ float np_pairwise_sum(const float* r) {
-  if constexpr (N < 8) {
-    float s = r[0];
-#pragma unroll
-    for (int i = 1; i < N; ++i) s = __fadd_rn(s, r[i]);
-    return s;
-  } else {
-    float p[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) p[i] = r[i];
-#pragma unroll
-    for (int i = 8; i + 8 <= N; i += 8) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) p[j] = __fadd_rn(p[j], r[i + j]);
-    }
-    float s = __fadd_rn(__fadd_rn(__fadd_rn(p[0], p[1]), __fadd_rn(p[2], p[3])),
-                        __fadd_rn(__fadd_rn(p[4], p[5]), __fadd_rn(p[6], p[7])));
-#pragma unroll
-    for (int i = (N / 8) * 8; i < N; ++i) s = __fadd_rn(s, r[i]);
-    return s;
-  }
-}
-
-template <int BD>
-__device__ __forceinline__ float dist_direct(const float* kk, const float* c) {
-  float r[BD];
-#pragma unroll
-  for (int j = 0; j < BD; ++j) {
-    float d = __fsub_rn(kk[j], c[j]);
-    r[j] = __fmul_rn(d, d);
-  }
-  return np_pairwise_sum<BD>(r);
-}
 
 struct AssignParams {
   const void* keys;
@@ -273,9 +238,31 @@ __global__ void vq_dequant_kernel(const uint8_t* idx, int64_t n_groups, int64_t 
 }  // namespace
 }  // namespace ss
 
+namespace ss {
+int launch_vq_assign_tc(const void* keys, int key_dtype, int64_t n_groups, int64_t rpg,
+                        int64_t kgs, int64_t krs, int d, const int32_t* perm,
+                        const float* cents, int bd, int k, const uint8_t* heavy,
+                        uint8_t* out_idx, int64_t igs, int64_t irs, uint16_t* out_heavy,
+                        int64_t hgs, int64_t hrs, float* out_pt, int dist_mode,
+                        cudaStream_t st);
+}  // namespace ss
+
 using namespace ss;
 
+namespace {
+// 0 = automatic, 1 = CUDA-core kernel only, 2 = tensor-core kernel required.
+int g_assign_path = 0;
+// Below this many rows the CUDA-core kernel has the lower latency.
+constexpr int64_t kTcMinRows = 512;
+}  // namespace
+
 extern "C" {
+
+int ss_set_assign_path(int path) {
+  SS_REQUIRE(path >= 0 && path <= 2, "ss_set_assign_path: path must be 0, 1 or 2");
+  g_assign_path = path;
+  return SS_OK;
+}
 
 int ss_vq_assign(const void* keys, int key_dtype, int64_t n_groups, int64_t rows_per_group,
                  int64_t key_group_stride, int64_t key_row_stride, int d, const int32_t* perm,
@@ -291,6 +278,19 @@ int ss_vq_assign(const void* keys, int key_dtype, int64_t n_groups, int64_t rows
   SS_REQUIRE(dist_mode == 0 || dist_mode == 1, "ss_vq_assign: bad dist_mode");
   count_dispatch("ss_vq_assign");
   if (n_groups <= 0 || rows_per_group <= 0) return SS_OK;
+  if (g_assign_path == 2 || (g_assign_path == 0 && n_groups * rows_per_group >= kTcMinRows)) {
+    const int rc = launch_vq_assign_tc(keys, key_dtype, n_groups, rows_per_group, key_group_stride,
+                                       key_row_stride, d, perm, centroids, bd, k, heavy, out_idx,
+                                       idx_group_stride, idx_row_stride, out_heavy,
+                                       heavy_group_stride, heavy_row_stride, out_pt, dist_mode,
+                                       as_stream(stream));
+    if (rc != SS_ERR_UNSUPPORTED) return rc;
+    if (g_assign_path == 2) {
+      return fail(SS_ERR_UNSUPPORTED,
+                  "ss_vq_assign: the tensor-core path needs bd in {4,8,16}, k a multiple of 32, "
+                  "d <= 128 and 16-byte aligned key rows");
+    }
+  }
   AssignParams p{keys, key_dtype, n_groups, rows_per_group, key_group_stride, key_row_stride,
                  d, d / bd, k, perm, centroids, heavy, out_idx, idx_group_stride,
                  idx_row_stride, out_heavy, heavy_group_stride, heavy_row_stride, out_pt,

@@ -105,6 +105,17 @@ def vq_assign(keys: torch.Tensor, centroids: torch.Tensor, *, perm: torch.Tensor
     return out_idx
 
 
+def set_assign_path(path: str = "auto") -> None:
+    """Selects the assignment kernel process-wide: "auto", "simt" (CUDA cores)
+    or "tensor" (tcgen05; raises for unsupported shapes). Results are identical."""
+    L.call("ss_set_assign_path", {"auto": 0, "simt": 1, "tensor": 2}[path])
+
+
+def assign_check(device=None) -> None:
+    """Synchronizes and raises if a tensor-core assignment pipeline wait timed out."""
+    L.call("ss_vq_assign_check", L.stream_ptr(device or torch.device("cuda")))
+
+
 def _collapsible(t: torch.Tensor) -> bool:
     """True if all dims before the last two collapse into one strided dim."""
     lead = t.shape[:-2]
