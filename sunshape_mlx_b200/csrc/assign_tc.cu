@@ -13,26 +13,38 @@
 //
 // with x = xh + xl the fp16 hi/lo split of a float32 value, after scaling the
 // block by a power of two so that its largest centroid component is in [1, 2).
-// The epilogue (one thread per row) keeps the smallest and second smallest V
-// with the centroid index packed into the low mantissa bits. Error analysis
-// (u = 2^-24, S = ||k||^2 + max_c ||c||^2, all in scaled units):
-//   |reference distance - exact real distance| <= 64u * S (both modes),
-//   |V - (exact distance - ||k||^2)|         <= 2^-16 * S (fp16 splits, the
-//        dropped kl*cl term, fp32 accumulation of <= 64 exact products),
-//   |packed V - V|                            <= 2^-14 * S (8 low bits).
-// So when second - first > 2^-12 * S no other centroid can have a reference
-// distance <= the winner's, and the winner is the reference's argmin. Rows
+// The epilogue (one thread per row) reads the row's V twice from TMEM: pass 1
+// takes the minimum s1 (three-input min, ALU pipe); pass 2 (FMA pipe)
+// evaluates e(c) = sat((s1 + T - V(c)) * 4/T), which is exactly 1 at the
+// minimum and exactly 0 for every V(c) >= s1 + T, and sums e and e * c.
+// A count of exactly 1 means no other centroid lies within T of the minimum,
+// and the summed position is the winner's index. Error analysis (u = 2^-24,
+// S = ||k||^2 + max_c ||c||^2, all in scaled units, per value; a comparison
+// of two values doubles each term):
+//   |reference distance - exact real distance| <= 2^-19 S (either mode),
+//   |V - (exact distance - ||k||^2)|         <= 2^-17 S (fp16 splits 2^-22,
+//        the dropped kl*cl term 2^-22, the csq split 2^-21, fp16 subnormals
+//        2^-20, and the fp32 accumulation of <= 26 exact products with one
+//        rounding or truncation of 2^-23 relative per addition, 2^-17.4).
+// Doubled and summed that is < 2^-15.5 S, and T = 2^-14 S. So when the count
+// is 1 no other centroid can have a reference distance <= the winner's, and
+// the winner is the reference's argmin. Rows
 // where that gap test fails (or whose values are not finite, or whose scaled
 // key does not fit fp16) are re-scored exactly by the whole warp in the
 // reference order, ties to the lowest index (np.argmin, kernels.py:1020).
 //
-// CTA roles (416 threads, one CTA per SM, persistent over row tiles):
+// CTA roles (384 threads, one CTA per SM, persistent over 128-row tiles of
+// one row group each):
 //   warps 0-7   epilogue: warp w reads TMEM lanes 32*(w%4)..+31; warps 0-3
 //               take even sequence steps (TMEM buffer 0), warps 4-7 odd ones
-//   warp 8      TMEM allocation; lane 0 issues the MMAs
-//   warps 9-12  producers: stage 128 key rows (coalesced 16-byte loads into a
-//               padded shared-memory tile), gather the permuted block, build
-//               the A operand in the canonical no-swizzle K-major layout
+//   warp 8      TMEM allocation; lane 0 of warps 0 and 4 issues its group's
+//               MMAs, whose completion frees the A slot and fills the TMEM
+//               buffer
+//   warps 9-10  producers: gather each row's permuted block from the staged
+//               key tile into the A operand (canonical no-swizzle K-major
+//               layout) and hand the scaled key norms to the epilogue
+//   warp 11     loader: stages key tiles (16-byte cp.async copies into a
+//               padded shared-memory tile) as far ahead as the ring allows
 // A sequence step is one (tile, block) pair; blocks of a CTA are a contiguous
 // group of the codec's blocks whose B operands stay resident in shared memory.
 #include "common.cuh"
@@ -45,12 +57,14 @@ __device__ unsigned int g_assign_status = 0;  // sticky: 1 = a pipeline wait gav
 namespace {
 
 constexpr int kTcRows = 128;            // MMA M (rows per tile)
+constexpr int kKnRing = 4;              // key-norm hand-off ring (producers -> epilogue)
 constexpr int kTcMmaWarp = 8;
 constexpr int kTcProdWarp0 = 9;
-constexpr int kTcProdThreads = 128;
-constexpr int kTcThreads = (kTcProdWarp0 * 32) + kTcProdThreads;  // 416
+constexpr int kTcProdThreads = 64;
+constexpr int kTcLoadWarp = kTcProdWarp0 + kTcProdThreads / 32;    // 12
+constexpr int kTcThreads = (kTcLoadWarp + 1) * 32;                  // 416
 constexpr uint64_t kTcWaitNs = 2000000000ull;                      // 2 s per wait
-constexpr float kTieRel = 1.0f / 4096.0f;                           // 2^-12
+constexpr float kTieRel = 1.0f / 16384.0f;                          // 2^-14
 
 struct TcParams {
   const void* keys;
@@ -68,10 +82,10 @@ struct TcParams {
   int dist_mode;
   int n_grp, gsize;       // block groups and blocks per group
   int slots;              // A ring depth
-  int64_t n_rows, n_tiles;
-  // dynamic shared-memory offsets (bytes)
-  uint32_t off_b, off_a, off_kn, off_stage, off_misc;
-  uint32_t stage_stride;  // bytes per staged row (d*es + 4)
+  int nstage;             // staged key tiles in flight (2 or 3)
+  int64_t tpg, n_tiles;   // 128-row tiles per group, total tiles
+  // dynamic shared-memory offsets (bytes, from the 1024-aligned base)
+  uint32_t off_b, off_a, off_stage, off_cf, off_misc, stage_bytes, stage_stride;
 };
 
 // ---- tcgen05 wrappers -------------------------------------------------------
@@ -145,14 +159,17 @@ __host__ __device__ constexpr uint32_t instr_desc_f16(int n) {
   return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kTcRows >> 4) << 24);
 }
 
-__device__ __forceinline__ uint32_t pack_halves(__half lo, __half hi) {
-  return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
-}
-
 template <int BD>
 struct TcShape {
   static constexpr int kKt = ((3 * BD + 2) + 15) / 16 * 16;  // K of the MMA chain
 };
+
+// fma with the result clamped to [0, 1] (NaN -> 0), on the FMA pipe.
+__device__ __forceinline__ float fma_sat(float a, float b, float c) {
+  float r;
+  asm("fma.rn.sat.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
 
 __device__ __forceinline__ float fmin3(float a, float b, float c) {
   float r;
@@ -186,33 +203,25 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile
   }
 }
 
-__device__ __forceinline__ void key_row_addr(const TcParams& p, int64_t r, int64_t& g,
-                                             int64_t& t) {
-  g = r / p.rpg;
-  t = r - g * p.rpg;
-}
-
 // Exact re-score of one (row, block) by the whole warp, reference order,
 // sequential '<' semantics of the reference loop: the first index whose
 // distance is below every earlier one; a NaN distance at index 0 keeps 0.
+// kk: the row's permuted block values (float32, unscaled); cb: the block's
+// float32 centroids in shared memory.
 template <int BD>
-__device__ int exact_rescan(const TcParams& p, const int16_t* s_perm, int64_t r, int b,
+__device__ int exact_rescan(const float (&kk)[BD], const float* cb, int k, int dist_mode,
                             int lane) {
-  int64_t g, t;
-  key_row_addr(p, r, g, t);
-  const int64_t base = g * p.kgs + t * p.krs;
-  float kk[BD];
-#pragma unroll
-  for (int j = 0; j < BD; ++j) kk[j] = load_as_f32(p.keys, p.key_dtype, base + s_perm[b * BD + j]);
-  const float* cb = p.cents + (size_t)b * p.k * BD;
   float best = __int_as_float(0x7f800000);
   int bi = 0x7fffffff;
   float d0 = 0.f;
-  for (int c = lane; c < p.k; c += 32) {
-    float cc[BD];
+  for (int c = lane; c < k; c += 32) {
+    float cv[BD];
 #pragma unroll
-    for (int j = 0; j < BD; ++j) cc[j] = __ldg(cb + (size_t)c * BD + j);
-    const float dd = p.dist_mode == 0 ? dist_direct<BD>(kk, cc) : dist_expanded<BD>(kk, cc);
+    for (int q = 0; q < BD; q += 4) {
+      const float4 f = *reinterpret_cast<const float4*>(cb + c * BD + q);
+      cv[q] = f.x; cv[q + 1] = f.y; cv[q + 2] = f.z; cv[q + 3] = f.w;
+    }
+    const float dd = dist_mode == 0 ? dist_direct<BD>(kk, cv) : dist_expanded<BD>(kk, cv);
     if (c == 0) d0 = dd;
     if (dd < best) { best = dd; bi = c; }
   }
@@ -227,26 +236,46 @@ __device__ int exact_rescan(const TcParams& p, const int16_t* s_perm, int64_t r,
   return bi;
 }
 
+// Element at byte column cb of tile row `row` in a staged key tile (rows
+// padded by 16 bytes so a column read by 32 consecutive rows hits 8 banks).
+__device__ __forceinline__ float stage_val(const uint8_t* st, uint32_t stride, int row, int cb,
+                                           int dt) {
+  const uint8_t* q = st + row * stride + cb;
+  if (dt == SS_F32) return *reinterpret_cast<const float*>(q);
+  const uint16_t u = *reinterpret_cast<const uint16_t*>(q);
+  return dt == SS_F16 ? h2f(u) : bf2f(u);
+}
+
 template <int BD>
-__global__ void __launch_bounds__(kTcThreads, 1) vq_assign_tc_kernel(TcParams p) {
-  extern __shared__ __align__(1024) uint8_t smem[];
+__global__ void __launch_bounds__(kTcThreads, 1)
+    vq_assign_tc_kernel(const __grid_constant__ TcParams p) {
+  extern __shared__ __align__(16) uint8_t smem[];
   uint8_t* s_b = smem + p.off_b;
   uint8_t* s_a = smem + p.off_a;
-  float* s_kn = reinterpret_cast<float*>(smem + p.off_kn);
   uint8_t* s_stage = smem + p.off_stage;
   uint8_t* misc = smem + p.off_misc;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(misc);              // 2*slots + 4
-  int16_t* s_perm = reinterpret_cast<int16_t*>(misc + 8 * 40);     // [d]
-  float* s_scale = reinterpret_cast<float*>(misc + 8 * 40 + 2048); // [gsize]
-  float* s_cmax = s_scale + 32;                                     // [gsize]
-  float* s_slo = s_cmax + 32;   // [gsize] scaled S below which fp32 distances may underflow
-  float* s_shi = s_slo + 32;    // [gsize] scaled S above which they may overflow
+  float* s_cf = reinterpret_cast<float*>(smem + p.off_cf);         // [gsize][k][BD] f32
+  uint64_t* bars = reinterpret_cast<uint64_t*>(misc);              // 2*slots + 10 + 16 (<= 32)
+  int16_t* s_pcol = reinterpret_cast<int16_t*>(misc + 256);        // [d] permuted column bytes
+  float* s_scale = reinterpret_cast<float*>(misc + 256 + 1024);    // [gsize]
+  float* s_cmax = s_scale + 32;  // [gsize] max scaled ||c||^2
+  float* s_slo = s_cmax + 32;    // [gsize] scaled S below which fp32 distances may underflow
+  float* s_shi = s_slo + 32;     // [gsize] scaled S above which they may overflow
   uint8_t* s_heavy = reinterpret_cast<uint8_t*>(s_shi + 32);        // [nb]
   uint8_t* s_hpos = s_heavy + 128;                                  // [nb]
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(s_hpos + 128);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
-  Bar bar{bars, bars + p.slots, bars + 2 * p.slots, bars + 2 * p.slots + 2};
+  uint64_t* a_full = bars;                 // [slots] producers -> MMA (64 arrivals)
+  uint64_t* a_empty = bars + p.slots;      // [slots] MMA commit -> producers
+  uint64_t* t_full = bars + 2 * p.slots;   // [2] MMA commit -> epilogue group
+  uint64_t* t_empty = t_full + 2;          // [2] epilogue group (4 warps) -> MMA
+  uint64_t* st_full = t_full + 4;          // [nstage] every loader lane's copies landed
+  uint64_t* st_empty = st_full + p.nstage; // [nstage] the producer warps are done with it
+  uint64_t* kn_full = st_empty + p.nstage; // [kKnRing] key norms of step n written (64)
+  uint64_t* kn_empty = kn_full + kKnRing;  // [kKnRing] read by the epilogue group (4 warps)
+  float* s_kn = reinterpret_cast<float*>(misc + 256 + 1024 + 4 * 32 * 4 + 256 + 16);  // [kKnRing][128]
+
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int grp = blockIdx.x % p.n_grp;
   const int b0 = grp * p.gsize;
@@ -254,9 +283,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) vq_assign_tc_kernel(TcParams p)
   constexpr int kt = TcShape<BD>::kKt;
   const uint32_t a_slot_bytes = kTcRows * kt * 2;
   const uint32_t b_blk_bytes = (uint32_t)p.k * kt * 2;
+  const int dt = p.key_dtype;
 
   // ---- setup: tables, barriers, TMEM, resident B operands -------------------
-  for (int i = tid; i < p.d; i += kTcThreads) s_perm[i] = (int16_t)(p.perm ? p.perm[i] : i);
+  for (int i = tid; i < p.d; i += kTcThreads) s_pcol[i] = (int16_t)((p.perm ? p.perm[i] : i) * p.es);
+  for (int i = tid; i < 32; i += kTcThreads) s_cmax[i] = 0.f;
   if (tid == 0) {
     int h = 0;
     for (int b = 0; b < p.nb; ++b) {
@@ -266,17 +297,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) vq_assign_tc_kernel(TcParams p)
       h += hv ? 1 : 0;
     }
     for (int s = 0; s < p.slots; ++s) {
-      mbar_init(bar.a_full + s, kTcProdThreads);
-      mbar_init(bar.a_empty + s, 4);
+      mbar_init(a_full + s, kTcProdThreads);
+      mbar_init(a_empty + s, 1);
     }
     for (int s = 0; s < 2; ++s) {
-      mbar_init(bar.t_full + s, 1);
-      mbar_init(bar.t_empty + s, 4);
+      mbar_init(t_full + s, 1);
+      mbar_init(t_empty + s, 4);
+    }
+    for (int s = 0; s < p.nstage; ++s) {
+      mbar_init(st_full + s, 32);
+      mbar_init(st_empty + s, kTcProdThreads / 32);
+    }
+    for (int s = 0; s < kKnRing; ++s) {
+      mbar_init(kn_full + s, kTcProdThreads);
+      mbar_init(kn_empty + s, 4);
     }
     *s_abort = 0;
     fence_mbar_init();
   }
-  for (int i = tid; i < 32; i += kTcThreads) s_cmax[i] = 0.f;
   // per-block scale: 2^(1 - e) with max |c| = m * 2^e, m in [0.5, 1)
   for (int bl = warp; bl < nbl; bl += kTcThreads / 32) {
     const float* cb = p.cents + (size_t)(b0 + bl) * p.k * BD;
@@ -304,6 +342,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) vq_assign_tc_kernel(TcParams p)
     tc_relinquish();
   }
   __syncthreads();
+  for (int i = tid; i < nbl * p.k * BD / 4; i += kTcThreads) {
+    reinterpret_cast<float4*>(s_cf)[i] =
+        reinterpret_cast<const float4*>(p.cents + (size_t)b0 * p.k * BD)[i];
+  }
   // B rows: [ch | cl | ch | csq_h, csq_l, 0...] per centroid, scaled
   for (int row = tid; row < nbl * p.k; row += kTcThreads) {
     const int bl = row / p.k, c = row - bl * p.k;
@@ -329,19 +371,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) vq_assign_tc_kernel(TcParams p)
     hv[3 * BD + 1] = __float2half_rn(csq - __half2float(ch));
 #pragma unroll
     for (int e = 0; e < kt; e += 2) {
-      __half2 pr = __halves2half2(hv[e], hv[e + 1]);
-      *reinterpret_cast<__half2*>(dst + kmaj_off(c, e, kt)) = pr;
+      *reinterpret_cast<__half2*>(dst + kmaj_off(c, e, kt)) = __halves2half2(hv[e], hv[e + 1]);
     }
     atomicMax(reinterpret_cast<int*>(s_cmax) + bl, __float_as_int(csq));  // csq >= 0
   }
-  // constant part of every A slot: elements [3*BD, kt) = 1, 1, 0, ...
+  // A slots: elements [2*BD, 3*BD) = 0 (stays 0 for fp16 keys), [3*BD, kt) = 1, 1, 0, ...
   for (int i = tid; i < p.slots * kTcRows; i += kTcThreads) {
     const int s = i / kTcRows, r = i - s * kTcRows;
     uint8_t* dst = s_a + (size_t)s * a_slot_bytes;
-    for (int e = 3 * BD; e < kt; e += 2) {
-      const __half lo = __float2half_rn(e == 3 * BD ? 1.f : 0.f);
-      const __half hi = __float2half_rn(e == 3 * BD ? 1.f : 0.f);
-      *reinterpret_cast<__half2*>(dst + kmaj_off(r, e, kt)) = __halves2half2(lo, hi);
+    for (int e = 2 * BD; e < kt; e += 2) {
+      const float v = e == 3 * BD ? 1.f : 0.f;
+      *reinterpret_cast<__half2*>(dst + kmaj_off(r, e, kt)) =
+          __halves2half2(__float2half_rn(v), __float2half_rn(v));
     }
   }
   fence_proxy_async_smem();
@@ -351,143 +392,121 @@ __global__ void __launch_bounds__(kTcThreads, 1) vq_assign_tc_kernel(TcParams p)
   const uint32_t tmem = *s_tmem;
 
   const int64_t tstride = gridDim.x / p.n_grp;
-  const int64_t t0 = blockIdx.x / p.n_grp;
+  const int64_t tfirst = blockIdx.x / p.n_grp;
 
-  if (warp >= kTcProdWarp0) {
+  if (warp >= kTcProdWarp0 && warp < kTcLoadWarp) {
     // ---------------------------------------------------------- producers
-    const int pt = tid - kTcProdWarp0 * 32;  // 0..127 = tile row
-    const uint32_t rb = (uint32_t)p.d * p.es, vr = rb / 16;
-    uint32_t n = 0;
+    const int pt = tid - kTcProdWarp0 * 32;  // rows pt, pt + 64 of the tile
+    uint32_t n = 0, li = 0;
     bool ok = true;
-    // After an abandoned wait the loops keep running without work so that
-    // every producer thread still reaches the same named barriers.
-    for (int64_t tile = t0; tile < p.n_tiles; tile += tstride) {
-      named_bar_sync(1, kTcProdThreads);  // previous tile's gathers are done
-      for (uint32_t v = pt; v < kTcRows * vr; v += kTcProdThreads) {
-        const uint32_t rr = v / vr, cv = v - rr * vr;
-        const int64_t r = tile * kTcRows + rr;
-        uint4 val = make_uint4(0, 0, 0, 0);
-        if (r < p.n_rows) {
-          int64_t g, t;
-          key_row_addr(p, r, g, t);
-          const uint8_t* src = reinterpret_cast<const uint8_t*>(p.keys) +
-                               (g * p.kgs + t * p.krs) * p.es + cv * 16;
-          val = __ldg(reinterpret_cast<const uint4*>(src));
-        }
-        uint32_t* dst = reinterpret_cast<uint32_t*>(s_stage + rr * p.stage_stride + cv * 16);
-        dst[0] = val.x; dst[1] = val.y; dst[2] = val.z; dst[3] = val.w;
-      }
-      named_bar_sync(1, kTcProdThreads);
-      const int64_t r = tile * kTcRows + pt;
-      const bool valid = r < p.n_rows;
-      const uint8_t* srow = s_stage + pt * p.stage_stride;
+    // After an abandoned wait the loops keep running without work.
+    for (int64_t tile = tfirst; tile < p.n_tiles; tile += tstride, ++li) {
+      const int sb = li % p.nstage;
+      if (ok) ok = tc_wait(st_full + sb, (li / p.nstage) & 1, s_abort);
+      const uint8_t* st = s_stage + (size_t)sb * p.stage_bytes;
       for (int bl = 0; bl < nbl; ++bl, ++n) {
         const int b = b0 + bl;
         const uint32_t slot = n % p.slots;
-        if (ok) ok = tc_wait(bar.a_empty + slot, ((n / p.slots) & 1) ^ 1, s_abort);
+        if (ok) ok = tc_wait(a_empty + slot, ((n / p.slots) & 1) ^ 1, s_abort);
+        if (ok) ok = tc_wait(kn_empty + n % kKnRing, ((n / kKnRing) & 1) ^ 1, s_abort);
         if (!ok) continue;
-        float x[BD];
+        uint8_t* dst = s_a + (size_t)slot * a_slot_bytes;
+        float* kn_out = s_kn + (n % kKnRing) * kTcRows;
+        const bool heavy = s_heavy[b] != 0;
+        const float sc = s_scale[bl];
+        for (int row = pt; row < kTcRows; row += kTcProdThreads) {
+          float x[BD];
 #pragma unroll
-        for (int j = 0; j < BD; ++j) {
-          const int dd = s_perm[b * BD + j];
-          if (p.es == 4) {
-            x[j] = *reinterpret_cast<const float*>(srow + dd * 4);
-          } else {
-            const uint16_t u = *reinterpret_cast<const uint16_t*>(srow + dd * 2);
-            x[j] = p.key_dtype == SS_F16 ? h2f(u) : bf2f(u);
-          }
-        }
-        if (s_heavy[b]) {
-          if (valid) {
-            int64_t g, t;
-            key_row_addr(p, r, g, t);
-            if (p.out_heavy) {
-              uint16_t* dst = p.out_heavy + g * p.hgs + t * p.hrs + s_hpos[b] * BD;
+          for (int j = 0; j < BD; ++j) x[j] = stage_val(st, p.stage_stride, row, s_pcol[b * BD + j], dt);
+          if (heavy) {
+            const int64_t g = tile / p.tpg;
+            const int64_t t = (tile - g * p.tpg) * kTcRows + row;
+            if (t < p.rpg) {
+              if (p.out_heavy) {
+                uint16_t* hd = p.out_heavy + g * p.hgs + t * p.hrs + s_hpos[b] * BD;
 #pragma unroll
-              for (int j = 0; j < BD; ++j) dst[j] = f2h(x[j]);
+                for (int j = 0; j < BD; ++j) hd[j] = f2h(x[j]);
+              }
+              if (p.out_pt) {
+                float* pd = p.out_pt + (g * p.rpg + t) * (int64_t)p.nb * BD + b * BD;
+#pragma unroll
+                for (int j = 0; j < BD; ++j) pd[j] = x[j];
+              }
             }
-            if (p.out_pt) {
-              float* dst = p.out_pt + r * (int64_t)p.nb * BD + b * BD;
-#pragma unroll
-              for (int j = 0; j < BD; ++j) dst[j] = x[j];
-            }
+            continue;
           }
-        } else {
-          const float sc = s_scale[bl];
+          // -2 * (x * sc) as fp16 hi (and lo unless the keys are fp16, whose
+          // power-of-two scaling is exact); the scaled squared key norm, NaN
+          // when a scaled value does not fit fp16 (forces the exact path)
+          uint32_t hw[BD / 2], lw[BD / 2];
           float kn = 0.f;
           bool fits = true;
-          __half ah[BD], al[BD];
 #pragma unroll
-          for (int j = 0; j < BD; ++j) {
-            const float xs = x[j] * sc;
-            kn = fmaf(xs, xs, kn);
-            fits = fits && (fabsf(xs) <= 32752.f);  // false for NaN / inf too
-            const __half h = __float2half_rn(xs);
-            const __half l = __float2half_rn(xs - __half2float(h));
-            ah[j] = __float2half_rn(-2.f * __half2float(h));
-            al[j] = __float2half_rn(-2.f * __half2float(l));
+          for (int j = 0; j < BD; j += 2) {
+            const float x0 = x[j] * sc, x1 = x[j + 1] * sc;
+            kn = fmaf(x1, x1, fmaf(x0, x0, kn));
+            fits = fits && fabsf(x0) <= 32752.f && fabsf(x1) <= 32752.f;  // false for NaN / inf
+            const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
+            hw[j / 2] = pack_h2(-2.f * __half2float(h0), -2.f * __half2float(h1));
+            if (dt != SS_F16) {
+              lw[j / 2] = pack_h2(-2.f * (x0 - __half2float(h0)), -2.f * (x1 - __half2float(h1)));
+            }
           }
-          uint8_t* dst = s_a + (size_t)slot * a_slot_bytes;
           if constexpr (BD % 8 == 0) {
 #pragma unroll
             for (int q = 0; q < BD; q += 8) {
-              uint4 hv, lv;
-              hv.x = pack_halves(ah[q], ah[q + 1]); hv.y = pack_halves(ah[q + 2], ah[q + 3]);
-              hv.z = pack_halves(ah[q + 4], ah[q + 5]); hv.w = pack_halves(ah[q + 6], ah[q + 7]);
-              lv.x = pack_halves(al[q], al[q + 1]); lv.y = pack_halves(al[q + 2], al[q + 3]);
-              lv.z = pack_halves(al[q + 4], al[q + 5]); lv.w = pack_halves(al[q + 6], al[q + 7]);
-              *reinterpret_cast<uint4*>(dst + kmaj_off(pt, q, kt)) = hv;
-              *reinterpret_cast<uint4*>(dst + kmaj_off(pt, BD + q, kt)) = hv;
-              *reinterpret_cast<uint4*>(dst + kmaj_off(pt, 2 * BD + q, kt)) = lv;
+              const uint4 hv = make_uint4(hw[q / 2], hw[q / 2 + 1], hw[q / 2 + 2], hw[q / 2 + 3]);
+              *reinterpret_cast<uint4*>(dst + kmaj_off(row, q, kt)) = hv;
+              *reinterpret_cast<uint4*>(dst + kmaj_off(row, BD + q, kt)) = hv;
+              if (dt != SS_F16) {
+                *reinterpret_cast<uint4*>(dst + kmaj_off(row, 2 * BD + q, kt)) =
+                    make_uint4(lw[q / 2], lw[q / 2 + 1], lw[q / 2 + 2], lw[q / 2 + 3]);
+              }
             }
           } else {
 #pragma unroll
             for (int q = 0; q < BD; q += 2) {
-              const uint32_t hv = pack_halves(ah[q], ah[q + 1]);
-              const uint32_t lv = pack_halves(al[q], al[q + 1]);
-              *reinterpret_cast<uint32_t*>(dst + kmaj_off(pt, q, kt)) = hv;
-              *reinterpret_cast<uint32_t*>(dst + kmaj_off(pt, BD + q, kt)) = hv;
-              *reinterpret_cast<uint32_t*>(dst + kmaj_off(pt, 2 * BD + q, kt)) = lv;
+              *reinterpret_cast<uint32_t*>(dst + kmaj_off(row, q, kt)) = hw[q / 2];
+              *reinterpret_cast<uint32_t*>(dst + kmaj_off(row, BD + q, kt)) = hw[q / 2];
+              if (dt != SS_F16) *reinterpret_cast<uint32_t*>(dst + kmaj_off(row, 2 * BD + q, kt)) = lw[q / 2];
             }
           }
-          s_kn[slot * kTcRows + pt] = fits ? kn : __int_as_float(0x7fc00000);
-          fence_proxy_async_smem();
+          kn_out[row] = fits ? kn : __int_as_float(0x7fc00000);
         }
-        mbar_arrive(bar.a_full + slot);
+        fence_proxy_async_smem();
+        mbar_arrive(a_full + slot);
+        mbar_arrive(kn_full + n % kKnRing);
       }
+      __syncwarp();
+      if (ok && lane == 0) mbar_arrive(st_empty + sb);
+    }
+  } else if (warp == kTcLoadWarp) {
+    // ---------------------------------------------------------- tile loader
+    // Stages key tiles as far ahead as the stage ring allows: 16-byte cp.async
+    // copies per lane (rows past the group's end read nothing and stage
+    // zeros), then one arrival per lane once its copies have landed.
+    const uint32_t vr = (uint32_t)p.d * p.es / 16;  // 16-byte chunks per key row
+    uint32_t li = 0;
+    for (int64_t tile = tfirst; tile < p.n_tiles; tile += tstride, ++li) {
+      const int buf = li % p.nstage;
+      const uint32_t use = li / p.nstage;
+      if (use > 0 && !__all_sync(0xffffffffu, tc_wait(st_empty + buf, (use - 1) & 1, s_abort))) break;
+      const int64_t g = tile / p.tpg;
+      const int64_t t0 = (tile - g * p.tpg) * kTcRows;
+      const uint8_t* src0 =
+          reinterpret_cast<const uint8_t*>(p.keys) + (g * p.kgs + t0 * p.krs) * p.es;
+      const uint32_t dst0 = smem_u32(s_stage + (size_t)buf * p.stage_bytes);
+      for (uint32_t v = lane; v < kTcRows * vr; v += 32) {
+        const uint32_t rr = v / vr, cv = v - rr * vr;
+        const bool in = t0 + rr < p.rpg;
+        cp_async16(dst0 + rr * p.stage_stride + cv * 16,
+                   in ? src0 + (int64_t)rr * p.krs * p.es + cv * 16 : src0, in ? 16u : 0u);
+      }
+      cp_async_mbar_arrive(st_full + buf);
     }
   } else if (warp == kTcMmaWarp) {
-    // ---------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc = instr_desc_f16(p.k);
-      const uint32_t sbo = kt * 16;
-      const uint32_t a0 = smem_u32(s_a), bb0 = smem_u32(s_b);
-      uint32_t n = 0;
-      bool ok = true;
-      for (int64_t tile = t0; tile < p.n_tiles && ok; tile += tstride) {
-        for (int bl = 0; bl < nbl; ++bl, ++n) {
-          const uint32_t slot = n % p.slots, buf = n & 1;
-          if (!tc_wait(bar.a_full + slot, (n / p.slots) & 1, s_abort)) { ok = false; break; }
-          if (!tc_wait(bar.t_empty + buf, ((n >> 1) & 1) ^ 1, s_abort)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t d_tmem = tmem + buf * 256;
-          const uint32_t a_addr = a0 + slot * a_slot_bytes;
-          const uint32_t b_addr = bb0 + bl * b_blk_bytes;
-          for (int j = 0; j < kt / 16; ++j) {
-            tc_mma_f16(d_tmem, smem_desc(a_addr + j * 256, 128, sbo),
-                       smem_desc(b_addr + j * 256, 128, sbo), idesc, j > 0 ? 1u : 0u);
-          }
-          tc_commit(bar.t_full + buf);
-        }
-      }
-      // Every issued MMA has completed once its buffer's last commit fired.
-      if (ok) {
-        for (uint32_t q = (n >= 2 ? n - 2 : 0); q < n; ++q) {
-          if (!tc_wait(bar.t_full + (q & 1), (q >> 1) & 1, s_abort)) break;
-        }
-      }
-    }
-    __syncwarp();
+    // TMEM owner: allocated above, released below; the epilogue groups
+    // issue their own MMAs.
   } else {
     // ---------------------------------------------------------- epilogue
     const int eg = warp >> 2;          // 0: even steps, 1: odd steps
@@ -495,68 +514,164 @@ __global__ void __launch_bounds__(kTcThreads, 1) vq_assign_tc_kernel(TcParams p)
     const int row = sub * 32 + lane;   // tile row of this thread
     const uint32_t tbase = tmem + ((uint32_t)(sub * 32) << 16) + eg * 256;
     const int nch = p.k / 32;
-    uint32_t n = 0;
+    const int64_t ntl = tfirst < p.n_tiles ? (p.n_tiles - tfirst + tstride - 1) / tstride : 0;
+    const uint32_t nsteps = (uint32_t)(ntl * nbl);
+    // Lane 0 of the group's first warp issues the group's MMAs (steps
+    // eg, eg + 2, ...) into the group's TMEM buffer, so neither group waits
+    // for the other.
+    const bool issuer = sub == 0 && lane == 0;
+    const uint32_t idesc = instr_desc_f16(p.k);
+    const uint32_t a0 = smem_u32(s_a), bb0 = smem_u32(s_b);
+    auto issue_mma = [&](uint32_t q) -> bool {
+      const uint32_t slot = q % p.slots;
+      const int qbl = (int)(q % nbl);
+      if (!tc_wait(t_empty + eg, ((q >> 1) & 1) ^ 1, s_abort)) return false;
+      if (!tc_wait(a_full + slot, (q / p.slots) & 1, s_abort)) return false;
+      tc_fence_after();
+      const uint32_t a_addr = a0 + slot * a_slot_bytes;
+      const uint32_t b_addr = bb0 + qbl * b_blk_bytes;
+#pragma unroll
+      for (int j = 0; j < kt / 16; ++j) {
+        tc_mma_f16(tmem + eg * 256, smem_desc(a_addr + j * 256, 128, kt * 16),
+                   smem_desc(b_addr + j * 256, 128, kt * 16), idesc, j > 0 ? 1u : 0u);
+      }
+      tc_commit(a_empty + slot);
+      tc_commit(t_full + eg);
+      return true;
+    };
     bool ok = true;
-    for (int64_t tile = t0; tile < p.n_tiles && ok; tile += tstride) {
-      const int64_t r = tile * kTcRows + row;
-      const bool valid = r < p.n_rows;
-      int64_t g = 0, t = 0;
-      if (valid) key_row_addr(p, r, g, t);
-      for (int bl = 0; bl < nbl; ++bl, ++n) {
-        if ((int)(n & 1) != eg) continue;
+    int64_t last = -1;  // last step this group's issuer launched
+    if (sub == 0) {
+      bool r = true;
+      if (issuer && (uint32_t)eg < nsteps) { r = issue_mma(eg); last = eg; }
+      ok = __shfl_sync(0xffffffffu, r, 0);
+    }
+    for (uint32_t n = eg; n < nsteps && ok; n += 2) {
+      const uint32_t li = n / nbl;
+      const int bl = (int)(n - li * nbl);
+      const int64_t tile = tfirst + (int64_t)li * tstride;
+      const int64_t g = tile / p.tpg;
+      const int64_t t = (tile - g * p.tpg) * kTcRows + row;
+      const bool valid = t < p.rpg;
+      {
         const int b = b0 + bl;
-        const uint32_t slot = n % p.slots;
-        ok = __all_sync(0xffffffffu, tc_wait(bar.t_full + eg, (n >> 1) & 1, s_abort));
+        ok = __all_sync(0xffffffffu, tc_wait(t_full + eg, (n >> 1) & 1, s_abort));
         if (!ok) break;
         tc_fence_after();
         const bool heavy = s_heavy[b] != 0;
-        float s1 = __int_as_float(0x7f800000), s2 = s1;
-        int c1chunk = 0;
+        int idx = 0;
+        bool need = false;
+        // the producers' scaled squared key norm of this row (NaN: exact path)
+        ok = __all_sync(0xffffffffu, tc_wait(kn_full + n % kKnRing, (n / kKnRing) & 1, s_abort));
+        if (!ok) break;
+        const float kn = s_kn[(n % kKnRing) * kTcRows + row];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(kn_empty + n % kKnRing);
         if (!heavy) {
-          for (int ch = 0; ch < nch; ++ch) {
-            uint32_t v[32];
-            tc_ld32(tbase + ch * 32, v);
+          // Pass 1 (ALU pipe): the row's minimum V, four independent chains,
+          // up to four 32-column chunks per TMEM wait.
+          const float inf = __int_as_float(0x7f800000);
+          float m0 = inf, m1 = inf, m2 = inf, m3 = inf;
+#pragma unroll 1
+          for (int ch = 0; ch < nch; ch += 4) {
+            const bool four = ch + 2 < nch;
+            uint32_t v0[32], v1[32], v2[32], v3[32];
+            tc_ld32(tbase + ch * 32, v0);
+            tc_ld32(tbase + (ch + 1) * 32, v1);
+            if (four) {
+              tc_ld32(tbase + (ch + 2) * 32, v2);
+              tc_ld32(tbase + (ch + 3) * 32, v3);
+            }
             tc_wait_ld();
-            const float old = s1;
 #pragma unroll
             for (int j = 0; j < 32; j += 2) {
-              const float a = __uint_as_float((v[j] & 0xFFFFFF00u) | (uint32_t)j);
-              const float c = __uint_as_float((v[j + 1] & 0xFFFFFF00u) | (uint32_t)(j + 1));
-              const float lo = fminf(a, c), hi = fmaxf(a, c);
-              s2 = fmin3(s2, hi, fmaxf(s1, lo));
-              s1 = fminf(s1, lo);
+              m0 = fmin3(m0, __uint_as_float(v0[j]), __uint_as_float(v0[j + 1]));
+              m1 = fmin3(m1, __uint_as_float(v1[j]), __uint_as_float(v1[j + 1]));
             }
-            if (s1 != old) c1chunk = ch;
+            if (four) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 2) {
+                m2 = fmin3(m2, __uint_as_float(v2[j]), __uint_as_float(v2[j + 1]));
+                m3 = fmin3(m3, __uint_as_float(v3[j]), __uint_as_float(v3[j + 1]));
+              }
+            }
           }
+          const float s1 = fminf(fmin3(m0, m1, m2), m3);
+          // Pass 2 (FMA pipe): e = sat((s1 + T - V) * 4/T) is exactly 1 at
+          // the minimum and exactly 0 for every V >= s1 + T (up to rounding
+          // of 2^-8 T); cnt = sum e, pos = sum e * column. cnt == 1 means no
+          // other centroid within T of the minimum and rint(pos) is its column.
+          // Chunk pairs are double-buffered: the next pair's TMEM load is in
+          // flight while the current one is summed.
+          const float sn = kn + s_cmax[bl];
+          const float tie = sn * kTieRel;
+          const float big = 4.f / tie;
+          const float thr_big = (s1 + tie) * big;
+          float cnt = 0.f, pos = 0.f;
+          auto sum_chunk = [&](const uint32_t (&v)[32], int ch) {
+            float ca = 0.f, pa = 0.f, cb = 0.f, pb = 0.f;
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) {
+              const float e = fma_sat(__uint_as_float(v[j]), -big, thr_big);
+              ca += e;
+              pa = fmaf(e, (float)j, pa);
+              const float e2 = fma_sat(__uint_as_float(v[j + 1]), -big, thr_big);
+              cb += e2;
+              pb = fmaf(e2, (float)(j + 1), pb);
+            }
+            cnt += ca + cb;
+            pos += fmaf(ca + cb, (float)(ch * 32), pa + pb);
+          };
+          {
+            uint32_t va[32], vb[32];
+            tc_ld32(tbase, va);
+            tc_wait_ld();
+#pragma unroll 1
+            for (int ch = 0; ch < nch; ch += 2) {
+              tc_ld32(tbase + (ch + 1) * 32, vb);  // nch is even
+              sum_chunk(va, ch);
+              tc_wait_ld();
+              if (ch + 2 < nch) tc_ld32(tbase + (ch + 2) * 32, va);
+              sum_chunk(vb, ch + 1);
+              tc_wait_ld();
+            }
+          }
+          need = valid && !(cnt == 1.f && sn >= s_slo[bl] && sn <= s_shi[bl]);
+          idx = min(max((int)rintf(pos), 0), p.k - 1);
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar.t_empty + eg);
-        // acquire the producer's key norms (that phase has already completed)
-        ok = __all_sync(0xffffffffu, tc_wait(bar.a_full + slot, (n / p.slots) & 1, s_abort));
-        if (!ok) break;
-        const float kn = s_kn[slot * kTcRows + row];
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar.a_empty + slot);
-        int idx = 0;
-        bool need = false;
-        if (!heavy) {
-          idx = c1chunk * 32 + (int)(__float_as_uint(s1) & 31u);
-          const float sn = kn + s_cmax[bl];
-          need = valid && !(s2 - s1 > sn * kTieRel && sn >= s_slo[bl] && sn <= s_shi[bl]);
+        if (lane == 0) mbar_arrive(t_empty + eg);
+        if (sub == 0) {
+          bool r = true;
+          if (issuer && n + 2 < nsteps) { r = issue_mma(n + 2); last = n + 2; }
+          ok = __shfl_sync(0xffffffffu, r, 0);
+          if (!ok) break;
         }
         uint32_t m = __ballot_sync(0xffffffffu, need);
+        // rows to re-score load their permuted block values (global memory,
+        // usually L2) all at once, then the warp scores them one by one
+        float kown[BD];
+        if (need) {
+          const int64_t base = g * p.kgs + t * p.krs;
+#pragma unroll
+          for (int j = 0; j < BD; ++j) kown[j] = load_as_f32(p.keys, dt, base + s_pcol[b * BD + j] / p.es);
+        }
         while (m) {
           const int src = __ffs(m) - 1;
           m &= m - 1;
-          const int64_t rr = tile * kTcRows + sub * 32 + src;
-          int bi;
-          bi = exact_rescan<BD>(p, s_perm, rr, b, lane);
+          float kk[BD];
+#pragma unroll
+          for (int j = 0; j < BD; ++j) kk[j] = __shfl_sync(0xffffffffu, kown[j], src);
+          const int bi = exact_rescan<BD>(kk, s_cf + (size_t)bl * p.k * BD, p.k, p.dist_mode, lane);
           if (lane == src) idx = bi;
         }
         if (valid) p.out_idx[g * p.igs + t * p.irs + b] = (uint8_t)idx;
       }
     }
+    // After an abandoned wait, let this group's launched MMAs finish before
+    // the TMEM is released (bounded).
+    if (!ok && issuer && last >= 0) mbar_wait_bounded(t_full + eg, (uint32_t)(last >> 1) & 1, 1000000ull);
   }
 
   tc_fence_before();
@@ -579,23 +694,31 @@ int launch_vq_assign_tc(const void* keys, int key_dtype, int64_t n_groups, int64
                         cudaStream_t st) {
   const int es = key_dtype == SS_F32 ? 4 : 2;
   if (!(bd == 4 || bd == 8 || bd == 16)) return SS_ERR_UNSUPPORTED;
-  if (k % 32 != 0 || k < 32 || k > 256) return SS_ERR_UNSUPPORTED;
-  if (d > 128 || (d * es) % 16 != 0) return SS_ERR_UNSUPPORTED;
+  if (k % 64 != 0 || k < 64 || k > 256) return SS_ERR_UNSUPPORTED;
+  if ((d * es) % 16 != 0 || d * es > 512) return SS_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(keys) & 15) != 0) return SS_ERR_UNSUPPORTED;
-  if (((kgs * es) & 15) != 0 || ((krs * es) & 15) != 0) return SS_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(cents) & 15) != 0) return SS_ERR_UNSUPPORTED;
+  if (((kgs * es) & 15) != 0 || ((krs * es) & 15) != 0 || krs < d) return SS_ERR_UNSUPPORTED;
   const int nb = d / bd;
   const int kt = bd == 4 ? TcShape<4>::kKt : bd == 8 ? TcShape<8>::kKt : TcShape<16>::kKt;
-  const uint32_t stage_stride = (uint32_t)(d * es + 4);
-  const uint32_t stage_bytes = (kTcRows * stage_stride + 127) / 128 * 128;
-  const uint32_t misc_bytes = 8 * 40 + 2048 + 4 * 32 * 4 + 256 + 16;
-  const uint32_t b_blk = (uint32_t)k * kt * 2, a_slot = kTcRows * kt * 2;
-  const uint32_t kn_slot = kTcRows * 4;
+  const uint32_t stage_stride = (uint32_t)(d * es + 16);
+  const uint32_t stage_bytes = kTcRows * stage_stride;
+  const uint32_t misc_bytes = 256 + 1024 + 4 * 32 * 4 + 256 + 16 + kKnRing * kTcRows * 4;
+  // per block: the B operand plus a float32 copy of the centroids (exact re-scans)
+  const uint32_t b_blk = (uint32_t)k * kt * 2, cf_blk = (uint32_t)k * bd * 4;
+  const uint32_t a_slot = kTcRows * kt * 2;
   const uint32_t limit = 227 * 1024;
-  int slots = 6, gsize = 0;
-  for (; slots >= 4; slots -= 2) {
-    const uint32_t fixed = slots * (a_slot + kn_slot) + stage_bytes + misc_bytes + 1024;
-    if (fixed < limit) gsize = (int)((limit - fixed) / b_blk);
-    if (gsize >= 1) break;
+  // Prefer 3 staged tiles and 3 A slots; shrink both for wide blocks / fp32 keys.
+  int nstage = 0, slots = 0, gsize = 0;
+  const int cand[4][2] = {{3, 3}, {2, 3}, {2, 2}, {1, 2}};
+  for (const auto& c : cand) {
+    const uint32_t fixed = c[1] * a_slot + c[0] * stage_bytes + misc_bytes;
+    const int gs = fixed < limit ? (int)((limit - fixed) / (b_blk + cf_blk)) : 0;
+    if (gs >= 2 || (gs >= 1 && c[0] == 1) || (gs >= nb)) {
+      nstage = c[0]; slots = c[1]; gsize = gs;
+      break;
+    }
+    if (gs >= 1 && gsize == 0) { nstage = c[0]; slots = c[1]; gsize = gs; }
   }
   if (gsize < 1) return SS_ERR_UNSUPPORTED;
   if (gsize > nb) gsize = nb;
@@ -609,20 +732,22 @@ int launch_vq_assign_tc(const void* keys, int key_dtype, int64_t n_groups, int64
   p.perm = perm; p.cents = cents; p.heavy = heavy; p.out_idx = out_idx;
   p.igs = igs; p.irs = irs; p.out_heavy = out_heavy; p.hgs = hgs; p.hrs = hrs;
   p.out_pt = out_pt; p.dist_mode = dist_mode;
-  p.n_grp = n_grp; p.gsize = gsize; p.slots = slots;
-  p.n_rows = n_groups * rpg;
-  p.n_tiles = (p.n_rows + kTcRows - 1) / kTcRows;
+  p.n_grp = n_grp; p.gsize = gsize; p.slots = slots; p.nstage = nstage;
+  p.tpg = (rpg + kTcRows - 1) / kTcRows;
+  p.n_tiles = n_groups * p.tpg;
   uint32_t off = 0;
+  p.off_stage = off; off += nstage * stage_bytes;   // 1024-aligned sizes first
   p.off_b = off; off += (uint32_t)gsize * b_blk;
   p.off_a = off; off += slots * a_slot;
-  p.off_kn = off; off += slots * kn_slot;
-  p.off_stage = off; off += stage_bytes;
+  p.off_cf = off; off += (uint32_t)gsize * cf_blk;
   p.off_misc = off; off += misc_bytes;
+  p.stage_bytes = stage_bytes;
   p.stage_stride = stage_stride;
   if (off > limit) return SS_ERR_UNSUPPORTED;
   // More than half an SM's shared memory: exactly one CTA (and one 512-column
   // TMEM allocation) per SM, so allocations never wait on each other.
-  const uint32_t smem = off < 120 * 1024 ? 120 * 1024 : off;
+  uint32_t smem = off;
+  if (smem < 120 * 1024) smem = 120 * 1024;
   int per_grp = sm_count() / n_grp;
   if (per_grp < 1) per_grp = 1;
   if (per_grp > p.n_tiles) per_grp = (int)p.n_tiles;
@@ -631,7 +756,7 @@ int launch_vq_assign_tc(const void* keys, int key_dtype, int64_t n_groups, int64
   case BDV:                                                                                 \
     cudaFuncSetAttribute(vq_assign_tc_kernel<BDV>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                          (int)smem);                                                        \
-    vq_assign_tc_kernel<BDV><<<grid, kTcThreads, smem, st>>>(p);                            \
+    vq_assign_tc_kernel<BDV><<<grid, kTcThreads, smem, st>>>(p);                       \
     break;
   switch (bd) {
     SS_LAUNCH_TC(4)

@@ -287,7 +287,7 @@ int ss_vq_assign(const void* keys, int key_dtype, int64_t n_groups, int64_t rows
     if (rc != SS_ERR_UNSUPPORTED) return rc;
     if (g_assign_path == 2) {
       return fail(SS_ERR_UNSUPPORTED,
-                  "ss_vq_assign: the tensor-core path needs bd in {4,8,16}, k a multiple of 32, "
+                  "ss_vq_assign: the tensor-core path needs bd in {4,8,16}, k a multiple of 64, "
                   "d <= 128 and 16-byte aligned key rows");
     }
   }

@@ -35,6 +35,12 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 const CUtensorMap* tmap_3d_f16_sw128(const void* base, uint64_t inner, uint64_t rows,
                                      uint64_t pairs, uint64_t pair_stride_bytes,
                                      uint32_t box_inner, uint32_t box_rows);
+// Same for any key dtype (SS_F16 / SS_BF16 / SS_F32) and an explicit row
+// stride (bytes): dims inner x rows x pairs.
+const CUtensorMap* tmap_3d_sw128(const void* base, int dtype, uint64_t inner, uint64_t rows,
+                                 uint64_t pairs, uint64_t row_stride_bytes,
+                                 uint64_t pair_stride_bytes, uint32_t box_inner,
+                                 uint32_t box_rows);
 
 // ---------------------------------------------------------------- device side
 __device__ __forceinline__ float h2f(uint16_t h) {
@@ -103,6 +109,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Non-blocking probe of a barrier phase.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n"
+      " mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
@@ -136,6 +154,19 @@ __device__ __forceinline__ void tma_load_3d(void* dst_smem, const CUtensorMap* m
       " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst_smem)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
       : "memory");
+}
+// 16-byte global -> shared copy (generic proxy, L2 only); src_bytes < 16
+// zero-fills the rest (0 = all zeros, nothing read).
+__device__ __forceinline__ void cp_async16(uint32_t dst_smem, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst_smem), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+// Arrives on the barrier once all of this thread's earlier cp.async copies
+// have landed (the arrival counts toward the barrier's expected count).
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
 }
 // Programmatic dependent launch: the primary grid allows its dependent to be
 // scheduled; the dependent waits for the primary's completion and memory.

@@ -71,13 +71,14 @@ EncodeTiledFn encode_fn() {
 }
 
 struct MapKey {
-  int dev;
+  int dev, dtype;
   const void* base;
-  uint64_t inner, rows, pairs, pair_stride;
+  uint64_t inner, rows, pairs, row_stride, pair_stride;
   uint32_t bi, br;
   bool operator<(const MapKey& o) const {
-    return std::tie(dev, base, inner, rows, pairs, pair_stride, bi, br) <
-           std::tie(o.dev, o.base, o.inner, o.rows, o.pairs, o.pair_stride, o.bi, o.br);
+    return std::tie(dev, dtype, base, inner, rows, pairs, row_stride, pair_stride, bi, br) <
+           std::tie(o.dev, o.dtype, o.base, o.inner, o.rows, o.pairs, o.row_stride,
+                    o.pair_stride, o.bi, o.br);
   }
 };
 std::mutex g_map_mu;
@@ -87,9 +88,18 @@ std::map<MapKey, CUtensorMap*> g_maps;
 const CUtensorMap* tmap_3d_f16_sw128(const void* base, uint64_t inner, uint64_t rows,
                                      uint64_t pairs, uint64_t pair_stride_bytes,
                                      uint32_t box_inner, uint32_t box_rows) {
+  return tmap_3d_sw128(base, SS_F16, inner, rows, pairs, inner * 2, pair_stride_bytes, box_inner,
+                       box_rows);
+}
+
+const CUtensorMap* tmap_3d_sw128(const void* base, int dtype, uint64_t inner, uint64_t rows,
+                                 uint64_t pairs, uint64_t row_stride_bytes,
+                                 uint64_t pair_stride_bytes, uint32_t box_inner,
+                                 uint32_t box_rows) {
   int dev = 0;
   cudaGetDevice(&dev);
-  MapKey key{dev, base, inner, rows, pairs, pair_stride_bytes, box_inner, box_rows};
+  MapKey key{dev, dtype, base, inner, rows, pairs, row_stride_bytes, pair_stride_bytes,
+             box_inner, box_rows};
   std::lock_guard<std::mutex> lk(g_map_mu);
   auto it = g_maps.find(key);
   if (it != g_maps.end()) return it->second;
@@ -104,10 +114,13 @@ const CUtensorMap* tmap_3d_f16_sw128(const void* base, uint64_t inner, uint64_t 
   }
   auto* m = new CUtensorMap;
   cuuint64_t dims[3] = {inner, rows, pairs};
-  cuuint64_t strides[2] = {inner * 2, pair_stride_bytes};
+  cuuint64_t strides[2] = {row_stride_bytes, pair_stride_bytes};
   cuuint32_t box[3] = {box_inner, box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides,
+  const CUtensorMapDataType dt = dtype == SS_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : dtype == SS_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                    : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(m, dt, 3, const_cast<void*>(base), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {

@@ -45,7 +45,7 @@ def _state(cents, perm=None, heavy=None):
 @pytest.mark.parametrize("bd,k,n,dt", [
     (8, 256, 4096, torch.float16), (8, 256, 1000, torch.float32), (8, 256, 777, torch.bfloat16),
     (4, 256, 1300, torch.float16), (16, 256, 600, torch.float32), (8, 64, 640, torch.float16),
-    (8, 96, 513, torch.float32), (4, 32, 900, torch.float16)])
+    (8, 128, 513, torch.float32), (4, 64, 900, torch.float16), (8, 192, 300, torch.float32)])
 def test_tensor_path_bit_exact(K, bd, k, n, dt):
     rng = np.random.default_rng(bd * 7919 + k * 31 + n)
     d = 128
