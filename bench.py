@@ -16,6 +16,11 @@ collective on the data path).
           store), sunshape_sdpa, device->host copy of the output.
 
 python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+python bench.py --assign [--assign-path tensor|simt] prints a second kind of
+line: the config-2 cache fill (16 x 8 x 8192 fp16 keys through codec.quantize's
+nearest-centroid assignment, ss_vq_assign), token-heads/s, with the oracle's
+CPU quantize beside it.
 """
 
 from __future__ import annotations
@@ -297,6 +302,102 @@ def run_ours(args, world, rank, local):
     return line
 
 
+# ---------------------------------------------------------------------- quantize (cache fill)
+def _assign_workload(device):
+    """cfg2 codec (fit on the CUDA-core path) and the 16 x 8 x 8192 key cache."""
+    import torch
+    import sunshape_mlx_b200 as ss
+    from sunshape_mlx_b200 import kernels as K
+
+    qc, kc, sig = _calibration()
+    K.set_assign_path("simt")  # the fit's own launches stay out of tensor-kernel captures
+    codec = ss.SunShapeBlockCodec(head_dim=D, block_dim=BD, n_centroids=KC, device=device)
+    codec.fit(qc, kc, kmeans_iters=25, seed=0)
+    K.set_assign_path("auto")
+    g = torch.Generator(device=device).manual_seed(4242)
+    keys = (torch.randn((B * HKV, T, D), generator=g, device=device)
+            * torch.tensor(sig, device=device)).half()
+    out = torch.empty((B * HKV, T, NB), dtype=torch.uint8, device=device)
+    return codec, keys, out
+
+
+def run_assign(args):
+    import torch
+    from sunshape_mlx_b200 import kernels as K
+    import oracle as O
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    codec, keys, out = _assign_workload(device)
+    perm = codec.permutation.to(device=device, dtype=torch.int32)
+    cents = codec.centroids.to(device)
+    K.set_assign_path(args.assign_path)
+
+    def step():
+        K.vq_assign(keys, cents, perm=perm, out_idx=out)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    if args.profile:
+        for _ in range(args.steps):
+            step()
+        torch.cuda.synchronize()
+        print("assign profile run done", flush=True)
+        return None
+    sampler = ClockSampler(_gpu_id(0))
+    sampler.start()
+    t_end = time.perf_counter() + 1.0
+    while time.perf_counter() < t_end:
+        for _ in range(20):
+            step()
+        torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(args.steps):
+        step()
+    e1.record(st)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    K.assign_check(device)
+    ms = e0.elapsed_time(e1) / args.steps
+    n_th = B * HKV * T
+    flops = 2.0 * KC * D * n_th  # ||c||^2 - 2k.c as a GEMM over all blocks
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak, peak_kind = float(json.load(f)["bf16_tflops"]), "measured (cuBLAS bf16 burst)"
+    except Exception:
+        peak, peak_kind = 1590.0, "fallback"
+    achieved = flops / (ms / 1e3) / 1e12
+    # CPU baseline: the oracle's NumPy quantize (the reference's CPU loop) on 8192 rows
+    st_np = {"mode": "profileperm_baseline", "head_dim": D, "block_dim": BD, "n_blocks": NB,
+             "n_centroids": KC, "centroids": codec.centroids.cpu().numpy(),
+             "permutation": codec.permutation.cpu().numpy(), "heavy": np.zeros(NB, bool)}
+    sample = keys[0, :8192].float().cpu().numpy()
+    t0 = time.perf_counter()
+    O.quantize(st_np, sample)
+    cpu_v = sample.shape[0] / (time.perf_counter() - t0)
+    return {
+        "metric": "block-VQ quantize (cache fill) token-heads/s", "value": n_th / (ms / 1e3),
+        "unit": "token-heads/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f16 keys, fp16 hi/lo GEMM + f32 exact re-score",
+        "data": "synthetic (seeded anisotropic fp16 keys)",
+        "config": {"workload": "cfg2 cache fill: 16 x 8 kv-heads x 8192 tokens, head_dim 128, "
+                               "bd 8, 256 centroids, ProfilePerm", "assign_path": args.assign_path,
+                   "l2": "inputs larger than L2 (268 MB of keys per step vs 126 MB L2)"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "peak_source": peak_kind,
+                     "note": "algorithmic 2*256*128 FLOP per token-head; the kernel is bound by "
+                             "its CUDA-core epilogue (profiles/vq_assign_tc_cfg2_cache_fill.md)"},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+        "cpu_baseline": {"value": cpu_v, "unit": "token-heads/s", "cores": os.cpu_count(),
+                         "kind": "port", "sample": "8192 rows of head 0 through the oracle's "
+                                                   "NumPy quantize (codec.py:472-514 loop)"},
+    }
+
+
 # ---------------------------------------------------------------------- reference arm
 def run_reference(args):
     """The reference's CPU path (oracle port of its NumPy quantize loop and
@@ -344,6 +445,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--assign", action="store_true",
+                    help="benchmark the cache-fill quantize (ss_vq_assign) instead of decode")
+    ap.add_argument("--assign-path", choices=["tensor", "simt", "auto"], default="tensor")
     ap.add_argument("--profile", action="store_true",
                     help="build the workload, run warmup+steps decode launches, exit "
                          "(short command for ncu captures)")
@@ -358,6 +462,11 @@ def main():
     import torch
     import torch.distributed as dist
 
+    if args.assign:
+        line = run_assign(args)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
     if world > 1:
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
