@@ -173,6 +173,73 @@ __global__ void kmeans_update_kernel(const float* data, int64_t n, int nb, int b
   }
 }
 
+// Same result with one CTA per block: a stable counting sort of the rows by
+// centroid (shared-memory histogram, then 32 rows per step with match-any
+// ranks so each centroid's rows keep their order), then one thread per
+// centroid sums its rows in that order.
+constexpr int kKmThreads = 256;
+constexpr int kKmMaxRowsSorted = 49152;  // row list in shared memory
+__global__ void __launch_bounds__(kKmThreads) kmeans_update_sorted_kernel(
+    const float* data, int n, int nb, int bd, const uint8_t* assign, const float* cin,
+    float* cout, int k) {
+  extern __shared__ int sm_km[];
+  int* s_cnt = sm_km;          // [256]
+  int* s_off = sm_km + 256;    // [256] running end offsets
+  int* s_list = sm_km + 512;   // [n] row ids grouped by centroid, rows in order
+  const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
+  for (int c = tid; c < 256; c += kKmThreads) s_cnt[c] = 0;
+  __syncthreads();
+  for (int i = tid; i < n; i += kKmThreads) atomicAdd(&s_cnt[assign[(int64_t)i * nb + b]], 1);
+  __syncthreads();
+  if (tid < 32) {
+    // exclusive scan of the 256 counts: 8 per lane
+    int loc[8], sum = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) { loc[q] = sum; sum += s_cnt[lane * 8 + q]; }
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    const int base = incl - sum;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) s_off[lane * 8 + q] = base + loc[q];
+    __syncwarp();
+    const unsigned lt = (1u << lane) - 1u;
+    for (int r0 = 0; r0 < n; r0 += 32) {
+      const int i = r0 + lane;
+      const int c = i < n ? (int)assign[(int64_t)i * nb + b] : 256 + lane;  // unique filler
+      const unsigned same = __match_any_sync(0xffffffffu, c);
+      if (i < n) s_list[s_off[c] + __popc(same & lt)] = i;
+      __syncwarp();
+      if (i < n && lane == 31 - __clz(same)) s_off[c] += __popc(same);
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  const int d = nb * bd;
+  for (int c = tid; c < k; c += kKmThreads) {
+    const int end = s_off[c], cnt = s_cnt[c];
+    float acc[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+    for (int q = end - cnt; q < end; ++q) {
+      const float* x = data + (int64_t)s_list[q] * d + b * bd;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        if (j < bd) acc[j] = __fadd_rn(acc[j], x[j]);
+      }
+    }
+    float* dst = cout + ((size_t)b * k + c) * bd;
+    const float* src = cin + ((size_t)b * k + c) * bd;
+    for (int j = 0; j < bd; ++j) {
+      dst[j] = cnt > 0 ? static_cast<float>(static_cast<double>(acc[j]) / static_cast<double>(cnt))
+                       : src[j];
+    }
+  }
+}
+
 // ------------------------------------------------------------------ scores
 // grid.x over token tiles of 256, grid.y over query chunks of 8; the LUT of
 // the chunk lives in shared memory.
@@ -333,6 +400,14 @@ int ss_kmeans_update(const float* data, int64_t n, int nb, int bd, const uint8_t
   SS_REQUIRE(cents_in != cents_out, "ss_kmeans_update: cents_in and cents_out alias");
   SS_REQUIRE(bd >= 1 && bd <= 16 && nb >= 1 && k >= 1 && k <= 256, "ss_kmeans_update: bad dims");
   count_dispatch("ss_kmeans_update");
+  if (n <= kKmMaxRowsSorted) {
+    const size_t smem = (512 + (size_t)n) * sizeof(int);
+    cudaFuncSetAttribute(kmeans_update_sorted_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+    kmeans_update_sorted_kernel<<<nb, kKmThreads, smem, as_stream(stream)>>>(
+        data, static_cast<int>(n), nb, bd, assign, cents_in, cents_out, k);
+    return check_launch("ss_kmeans_update");
+  }
   const int threads = 128;
   const int blocks = (nb * k + threads - 1) / threads;
   kmeans_update_kernel<<<blocks, threads, 0, as_stream(stream)>>>(data, n, nb, bd, assign,

@@ -119,6 +119,27 @@ def test_kmeans_update_bit_exact(ss):
         np.testing.assert_array_equal(out[b].cpu().numpy(), want)
 
 
+@pytest.mark.parametrize("n,bd,k", [(30000, 4, 256), (777, 16, 64), (50000, 8, 256)])
+def test_kmeans_update_bit_exact_sizes(ss, n, bd, k):
+    """Sorted (n <= 49152) and scanning (larger n) update kernels, np.add.at order."""
+    from sunshape_mlx_b200 import _lib as L
+
+    rng = np.random.default_rng(n + bd)
+    nb = 128 // bd
+    x = rng.standard_normal((n, nb * bd)).astype(np.float32)
+    cin = rng.standard_normal((nb, k, bd)).astype(np.float32)
+    assign = rng.integers(0, k - 5, (n, nb)).astype(np.uint8)
+    assign[: n // 3, 0] = 7  # one heavily used cluster
+    xt, at, ct = (torch.tensor(a, device="cuda") for a in (x, assign, cin))
+    out = torch.empty_like(ct)
+    L.call("ss_kmeans_update", L.ptr(xt), n, nb, bd, L.ptr(at), L.ptr(ct), L.ptr(out), k,
+           L.stream_ptr())
+    got = out.cpu().numpy()
+    for b in range(nb):
+        want = O.kmeans_update(x[:, b * bd:(b + 1) * bd], assign[:, b].astype(np.int64), cin[b])
+        np.testing.assert_array_equal(got[b], want)
+
+
 def test_kmeans_expanded_assignment_matches_blas_form(ss):
     from sunshape_mlx_b200 import kernels as K
 
