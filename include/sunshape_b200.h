@@ -85,7 +85,7 @@ int ss_vq_assign(const void* keys, int key_dtype, int64_t n_groups, int64_t rows
 
 /* Assignment kernel selection (no counterpart in the reference, which has one
  * CPU loop and one Metal kernel): 0 = automatic (tensor-core kernel for
- * >= 512 rows when bd in {4,8,16}, k in {64,128,192,256}, d <= 128 and key rows are
+ * >= 16384 rows when bd in {4,8,16}, k in {64,128,192,256}, d <= 128 and key rows are
  * 16-byte aligned; CUDA-core kernel otherwise), 1 = CUDA-core kernel only,
  * 2 = tensor-core kernel or SS_ERR_UNSUPPORTED. Process-wide. Both kernels
  * return the same indices. */

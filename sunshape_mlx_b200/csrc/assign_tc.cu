@@ -61,8 +61,8 @@ constexpr int kKnRing = 4;              // key-norm hand-off ring (producers -> 
 constexpr int kTcMmaWarp = 8;
 constexpr int kTcProdWarp0 = 9;
 constexpr int kTcProdThreads = 64;
-constexpr int kTcLoadWarp = kTcProdWarp0 + kTcProdThreads / 32;    // 12
-constexpr int kTcThreads = (kTcLoadWarp + 1) * 32;                  // 416
+constexpr int kTcLoadWarp = kTcProdWarp0 + kTcProdThreads / 32;    // 11
+constexpr int kTcThreads = (kTcLoadWarp + 1) * 32;                  // 384
 constexpr uint64_t kTcWaitNs = 2000000000ull;                      // 2 s per wait
 constexpr float kTieRel = 1.0f / 16384.0f;                          // 2^-14
 

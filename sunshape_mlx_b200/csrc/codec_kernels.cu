@@ -320,7 +320,7 @@ namespace {
 // 0 = automatic, 1 = CUDA-core kernel only, 2 = tensor-core kernel required.
 int g_assign_path = 0;
 // Below this many rows the CUDA-core kernel has the lower latency.
-constexpr int64_t kTcMinRows = 512;
+constexpr int64_t kTcMinRows = 16384;
 }  // namespace
 
 extern "C" {
