@@ -17,6 +17,11 @@ collective on the data path).
 
 python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
+python bench.py --config 3 | 5 times the other two decode configurations
+(config 3: B=64, T_kv=32768, 2-bit TurboQuant-style values with fp16 per-group
+scales; config 5: B=1, 64q/8kv, T_kv=524288 mixed-precision keys, split-KV
+across the torchrun ranks with an NCCL all-gather + log-sum-exp merge).
+
 python bench.py --assign [--assign-path tensor|simt] prints a second kind of
 line: the config-2 cache fill (16 x 8 x 8192 fp16 keys through codec.quantize's
 nearest-centroid assignment, ss_vq_assign), token-heads/s, with the oracle's
@@ -302,6 +307,172 @@ def run_ours(args, world, rank, local):
     return line
 
 
+# ---------------------------------------------------------------------- configs 3 and 5
+CFG3 = dict(B=64, HQ=32, HKV=8, T=32768, bytes_per_th=NB + 32 + 8,
+            workload="cfg3: hybrid-cache decode, B=64/GPU, 32q/8kv heads, head_dim 128, T_kv 32768, "
+                     "SunShape 1-bit keys + 2-bit TurboQuant-style values (rotated, Lloyd-Max levels, "
+                     "fp16 scale per 32 channels), buffer_size 0, 1 query token/step")
+CFG5 = dict(B=1, HQ=64, HKV=8, T=524288, bytes_per_th=12 + 4 * BD * 2 + 2 * D,
+            workload="cfg5: long-context decode, B=1, 64q/8kv heads, head_dim 128, T_kv 524288, "
+                     "profileperm_mixed_precision keys (4 of 16 blocks fp16, 12 VQ'd), fp16 values, "
+                     "prefill-quantised in 32768-token chunks, T_kv split across ranks")
+
+
+def _build_cfg3(device):
+    import torch
+    import sunshape_mlx_b200 as ss
+
+    c = CFG3
+    qc, kc, sig = _calibration()
+    codec = ss.SunShapeBlockCodec(head_dim=D, block_dim=BD, n_centroids=KC, device=device)
+    codec.fit(qc, kc, kmeans_iters=25, seed=0)
+    cache = ss.create_kv_cache(codec, n_kv_heads=c["HKV"], value_backend="turboquant",
+                               value_bits=2, tq_group_size=32, buffer_size=0)
+    g = torch.Generator(device=device).manual_seed(31)
+    sig_t = torch.tensor(sig, device=device)
+    for _ in range(c["T"] // 2048):
+        k = (torch.randn((c["B"], c["HKV"], 2048, D), generator=g, device=device) * sig_t).half()
+        v = torch.randn((c["B"], c["HKV"], 2048, D), generator=g, device=device).half()
+        cache.append(k, v)
+    del k, v
+    q = torch.randn((c["B"], c["HQ"], 1, D), generator=g, device=device).half()
+    return codec, cache, q
+
+
+def _build_cfg5(device, rank, world):
+    """This rank's contiguous token range of the config-5 sequence."""
+    import torch
+    import sunshape_mlx_b200 as ss
+    from sunshape_mlx_b200 import splitkv
+
+    c = CFG5
+    qc, kc, sig = _calibration()
+    codec = ss.SunShapeBlockCodec(head_dim=D, block_dim=BD, n_centroids=KC, device=device,
+                                  mode="profileperm_mixed_precision", n_heavy=4)
+    codec.fit(qc, kc, kmeans_iters=25, seed=0)
+    cache = ss.create_kv_cache(codec, n_kv_heads=c["HKV"])
+    lo, hi = splitkv.shard_range(c["T"], rank, world)
+    sig_t = torch.tensor(sig, device=device)
+    chunk = 32768
+    for a in range(0, c["T"], chunk):  # the same sequence on every rank; keep this shard
+        if a + chunk <= lo or a >= hi:
+            continue
+        g = torch.Generator(device=device).manual_seed(5000 + a // chunk)
+        k = (torch.randn((1, c["HKV"], chunk, D), generator=g, device=device) * sig_t).half()
+        v = torch.randn((1, c["HKV"], chunk, D), generator=g, device=device).half()
+        s0, s1 = max(lo, a) - a, min(hi, a + chunk) - a
+        cache.append(k[:, :, s0:s1].contiguous(), v[:, :, s0:s1].contiguous())
+    g = torch.Generator(device=device).manual_seed(777)
+    q = torch.randn((1, c["HQ"], 1, D), generator=g, device=device).half()
+    return codec, cache, q
+
+
+def run_config(args, world, rank, local):
+    import torch
+    import torch.distributed as dist
+    from sunshape_mlx_b200.attention import PreparedDecode
+    from sunshape_mlx_b200 import splitkv
+
+    c = CFG3 if args.config == 3 else CFG5
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    scale = 1 / math.sqrt(D)
+    if args.config == 3:
+        codec, cache, q = _build_cfg3(device)
+    else:
+        codec, cache, q = _build_cfg5(device, rank, world)
+    if world > 1 and args.config == 5:
+        def step():
+            splitkv.splitkv_sdpa(q, cache, scale)
+        launches = 3  # table + decode (partials) + merge; plus the NCCL all-gather
+    else:
+        prep = PreparedDecode(q, cache, scale)
+        step = prep.run
+        launches = 2
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    sampler = ClockSampler(_gpu_id(local))
+    sampler.start()
+    t_end = time.perf_counter() + 1.0
+    while time.perf_counter() < t_end:
+        for _ in range(20):
+            step()
+        torch.cuda.synchronize()
+    barrier()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(args.steps):
+        step()
+    e1.record(st)
+    barrier()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    ms_t = torch.tensor([ms], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t)
+    if rank != 0:
+        return None
+    peak, peak_kind = _peaks()
+    per_rank_tokens = c["T"] // world if args.config == 5 else c["T"]
+    alg_bytes = c["B"] * c["HKV"] * per_rank_tokens * c["bytes_per_th"] + 2 * c["B"] * c["HQ"] * D * 2
+    achieved = alg_bytes / (ms / 1e3) / 1e9
+    nq = c["B"] * c["HQ"] * (world if args.config == 3 else 1)
+    line = {
+        "metric": METRIC, "value": nq / (ms / 1e3), "unit": "queries/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak" if args.config == 3 else "strong", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded anisotropic keys, N(0,1) fp16 values/queries)",
+        "config": {"workload": c["workload"], "global_batch": c["B"] * (world if args.config == 3 else 1),
+                   "seq_len": c["T"], "parallelism": (f"dp{world} (batch shards)" if args.config == 3
+                                                      else f"split-KV x{world} (token shards, NCCL all-gather + LSE merge)"),
+                   "l2": f"inputs larger than L2 ({alg_bytes / 1e6:.0f} MB streamed per step per GPU)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_source": peak_kind,
+                     "frac_of_8TBs_nominal": achieved / 8000.0, "traffic": None,
+                     "algorithmic_bytes_per_launch": alg_bytes,
+                     "bytes_per_token_head": c["bytes_per_th"]},
+        "gpu_launches": launches * args.steps,
+        "clocks": clocks,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = _cpu_baseline_cfg(args.config, codec, cache, q)
+    return line
+
+
+def _cpu_baseline_cfg(cfg, codec, cache, q, budget_s: float = 8.0):
+    """Oracle CPU path on one kv-head of batch row 0 (its n_rep query heads):
+    the reference dequantises the values and runs its 2-pass SDPA."""
+    import oracle as O
+
+    st = codec.state_dict()
+    state = {"mode": "profileperm_baseline", "head_dim": D, "block_dim": BD, "n_blocks": NB,
+             "n_centroids": KC, "centroids": st["centroids"].numpy(),
+             "permutation": st["permutation"].numpy(), "heavy": np.zeros(NB, bool)}
+    c = CFG3 if cfg == 3 else CFG5
+    rep = c["HQ"] // c["HKV"]
+    idx = cache.key_indices[:1, :1].cpu().numpy()
+    vals = cache.values[:1, :1].float().cpu().numpy()  # dequantised as the reference does
+    qn = q[:1, :rep].float().cpu().numpy()
+    n, t0 = 0, time.perf_counter()
+    while True:
+        O.sdpa(qn, state, idx, vals, 1 / math.sqrt(D))
+        n += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": rep * n / dt, "unit": "queries/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{n} x decode of {rep} query heads over 1 kv-head x {idx.shape[2]} tokens "
+                      "(batch row 0), oracle NumPy 2-pass path on dequantised values, all host cores"}
+
+
 # ---------------------------------------------------------------------- quantize (cache fill)
 def _assign_workload(device):
     """cfg2 codec (fit on the CUDA-core path) and the 16 x 8 x 8192 key cache."""
@@ -445,6 +616,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", type=int, choices=[2, 3, 5], default=2,
+                    help="decode configuration (BASELINE configs 2, 3, 5)")
     ap.add_argument("--assign", action="store_true",
                     help="benchmark the cache-fill quantize (ss_vq_assign) instead of decode")
     ap.add_argument("--assign-path", choices=["tensor", "simt", "auto"], default="tensor")
@@ -470,6 +643,15 @@ def main():
     if world > 1:
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    if args.config != 2:
+        try:
+            line = run_config(args, world, rank, local)
+            if line is not None:
+                print(json.dumps(line), flush=True)
+        finally:
+            if world > 1:
+                dist.destroy_process_group()
+        return
     if args.profile:
         from sunshape_mlx_b200.attention import PreparedDecode
 

@@ -129,6 +129,7 @@ struct Misc {  // small shared-memory state
   float o[8][128];      // finalisation staging
   float mrow[8], lrow[8];
   float levels[16];
+  float2 lvpair[16];    // 2-bit values: levels of the two codes of each 4-bit nibble
   int heavy_pos[32];
   uint8_t is_heavy[128];
   int is_last;
@@ -284,6 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
       if (hv && hp < 32) ms.heavy_pos[hp++] = b;
     }
     for (int i = 0; i < 16; ++i) ms.levels[i] = p.levels[i];
+    for (int i = 0; i < 16; ++i) ms.lvpair[i] = make_float2(p.levels[i & 3], p.levels[i >> 2]);
     fence_mbar_init();
   }
   __syncthreads();
@@ -653,7 +655,39 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
         const uint32_t vb = smem_u32(vdq_w) + kk_off * 128;
         for (int ks = 0; ks < SL / 16; ++ks) {
           // decode 16 tokens of the slice into this warp's fp16 staging tile
-          if (compressed) {
+          if (compressed && D == 128 && p.v_bits == 2 && p.v_group % 16 == 0) {
+            // 2-bit codes: lane = (token, half row); four 16-value words per
+            // lane in one 16-byte load, one nibble -> two levels per lookup
+            const uint8_t* sp = st + p.off_aux + TILE * p.v_words * 4;
+            const float* zp = p.vz ? reinterpret_cast<const float*>(
+                                         sp + TILE * p.v_groups * (p.vs_dt == SS_F32 ? 4 : 2))
+                                   : nullptr;
+            const int tk = lane >> 1, hw = lane & 1;
+            const int tt = slice * SL + ks * 16 + tk;
+            const uint4 wv = *reinterpret_cast<const uint4*>(st + p.off_aux + (tt * 8 + hw * 4) * 4);
+            const uint32_t wrd[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi) {
+              const int w = hw * 4 + wi;  // dims 16w .. 16w + 15
+              const int gi = (w * 16) / p.v_group;
+              const float s_ = p.vs_dt == SS_F32
+                                   ? reinterpret_cast<const float*>(sp)[tt * p.v_groups + gi]
+                                   : h2f(reinterpret_cast<const uint16_t*>(sp)[tt * p.v_groups + gi]);
+              const float z_ = zp ? zp[tt * p.v_groups + gi] : 0.f;
+              uint32_t h[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float2 lv = ms.lvpair[(wrd[wi] >> (4 * j)) & 15u];
+                float x0 = __fmul_rn(lv.x, s_), x1 = __fmul_rn(lv.y, s_);
+                if (zp) { x0 = __fadd_rn(x0, z_); x1 = __fadd_rn(x1, z_); }
+                h[j] = pack_h2(x0, x1);
+              }
+              *reinterpret_cast<uint4*>(vdq_w + vtile_addr(0, 16, tk, w * 16)) =
+                  make_uint4(h[0], h[1], h[2], h[3]);
+              *reinterpret_cast<uint4*>(vdq_w + vtile_addr(0, 16, tk, w * 16 + 8)) =
+                  make_uint4(h[4], h[5], h[6], h[7]);
+            }
+          } else if (compressed) {
             const uint32_t* words = reinterpret_cast<const uint32_t*>(st + p.off_aux);
             const uint8_t* sp = st + p.off_aux + TILE * p.v_words * 4;
             const float* zp = p.vz ? reinterpret_cast<const float*>(
@@ -882,7 +916,7 @@ struct Plan {
 
 constexpr size_t kSmemBudget = 226 * 1024;  // leaves room for static barriers
 
-int make_plan(const ss_decode_args* a, Plan& pl) {
+int make_plan_r(const ss_decode_args* a, Plan& pl, int r_cap) {
   SS_REQUIRE(a, "ss_decode_attn: null args");
   SS_REQUIRE(a->d == 64 || a->d == 128, "ss_decode_attn: head_dim must be 64 or 128");
   SS_REQUIRE(a->bd > 0 && a->bd <= 16 && a->d % a->bd == 0, "ss_decode_attn: bad block_dim");
@@ -896,7 +930,7 @@ int make_plan(const ss_decode_args* a, Plan& pl) {
   const int nrep = a->hq / a->hkv;
   const int rows = nrep * a->tq;
   int R = rows >= 5 ? 8 : (rows >= 3 ? 4 : (rows == 2 ? 2 : 1));
-  while (R > 1 && (size_t)nb * a->k * R * 4 > 128 * 1024) R >>= 1;
+  while (R > r_cap || (R > 1 && (size_t)nb * a->k * R * 4 > 128 * 1024)) R >>= 1;
   pl.R = R;
   pl.tile = 128;
   SS_REQUIRE(nb % 2 == 0 && nb <= 128, "ss_decode_attn: n_blocks must be even and <= 128");
@@ -976,6 +1010,15 @@ int make_plan(const ss_decode_args* a, Plan& pl) {
                  ~size_t(255);
   pl.ws_bytes = pl.off_lut_g + (size_t)pl.n_units * pl.lut_unit_bytes;
   return SS_OK;
+}
+
+// Largest row group that fits: 8 query rows per unit need a 128 KB table next
+// to the stage ring; when that does not fit (wide stages, e.g. heavy key
+// blocks) the rows are split into groups of 4, which streams the unit twice.
+int make_plan(const ss_decode_args* a, Plan& pl) {
+  int rc = make_plan_r(a, pl, 8);
+  if (rc == SS_ERR_UNSUPPORTED && pl.R == 8) rc = make_plan_r(a, pl, 4);
+  return rc;
 }
 
 template <int R, int D>
