@@ -213,6 +213,14 @@ __device__ __forceinline__ void mma_16816(float* d, uint32_t a0, uint32_t a1, ui
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// (a, b) += (x, y) as one packed fp32 add (two round-to-nearest fp32 adds).
+__device__ __forceinline__ void add_f32x2(float& a, float& b, float x, float y) {
+  asm("{\n .reg .b64 t, u;\n mov.b64 t, {%0, %1};\n mov.b64 u, {%2, %3};\n"
+      " add.rn.f32x2 t, t, u;\n mov.b64 {%0, %1}, t;\n}"
+      : "+f"(a), "+f"(b)
+      : "f"(x), "f"(y));
+}
+
 __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);

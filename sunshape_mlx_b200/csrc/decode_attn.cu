@@ -506,10 +506,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
 #pragma unroll
                 for (int r4 = 0; r4 < R; r4 += 4) {
                   const float4 a4 = *reinterpret_cast<const float4*>(e0 + r4);
-                  s0[r4] += a4.x; s0[r4 + 1] += a4.y; s0[r4 + 2] += a4.z; s0[r4 + 3] += a4.w;
+                  add_f32x2(s0[r4], s0[r4 + 1], a4.x, a4.y);
+                  add_f32x2(s0[r4 + 2], s0[r4 + 3], a4.z, a4.w);
                   if (TPL > 1) {
                     const float4 b4 = *reinterpret_cast<const float4*>(e1 + r4);
-                    s1[r4] += b4.x; s1[r4 + 1] += b4.y; s1[r4 + 2] += b4.z; s1[r4 + 3] += b4.w;
+                    add_f32x2(s1[r4], s1[r4 + 1], b4.x, b4.y);
+                    add_f32x2(s1[r4 + 2], s1[r4 + 3], b4.z, b4.w);
                   }
                 }
               } else {

@@ -212,7 +212,8 @@ def test_quantized_values_decode_vs_torch(ss):
         assert G.rel_err(out, want) < 2e-3, (kind, G.rel_err(out, want))
 
 
-def test_mixed_precision_heavy_blocks_exact_scoring(ss):
+@pytest.mark.parametrize("hq", [8, 16])  # 16: 8 rows per kv-head, tables split into 2 row groups
+def test_mixed_precision_heavy_blocks_exact_scoring(ss, hq):
     rng = np.random.default_rng(4)
     qc = I.heavy_tailed_queries(2048, 128, seed=7)
     kc = rng.standard_normal((2048, 128)).astype(np.float32)
@@ -222,7 +223,7 @@ def test_mixed_precision_heavy_blocks_exact_scoring(ss):
     cache = ss.create_kv_cache(codec, n_kv_heads=2)
     kk, vv = I.kv_stream(8, 1, 2, 700, 128)
     cache.update_and_fetch(kk, vv)
-    q = I.decode_queries(9, 1, 8, 1, 128)
+    q = I.decode_queries(9, 1, hq, 1, 128)
     out = ss.sunshape_sdpa(q, cache, 1 / math.sqrt(128))
     # reference semantics with heavy blocks restored: q . dequantize(quantize(k))
     khat = torch.stack([torch.stack([codec(torch.tensor(kk[0, h], device="cuda")) for h in range(2)])])
