@@ -32,9 +32,10 @@
 namespace ss {
 namespace {
 
-constexpr int kConsumerWarps = 8;
-constexpr int kConsumers = kConsumerWarps * 32;
-constexpr int kThreads = kConsumers + 32;
+// Consumer warps per CTA (CW, a kernel template parameter): 8 with 4 stages
+// of 128 tokens, or 12 with 6 stages when the stage is small (quantized
+// values); one producer warp follows them.
+constexpr int kLutThreads = 256;  // table kernel block size
 constexpr int kMaxStages = 8;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per barrier wait
 constexpr float kLog2e = 1.4426950408889634f;
@@ -44,7 +45,7 @@ struct DecodeParams {
   int b, hq, hkv, tq, d, nb, bd, k, nrep, n_heavy;
   int R, tile, n_rg, n_ct, n_tt, tpu;
   int64_t tc, ttail, total_tiles, n_units;
-  int grid, stages, stage_shift, max_cov;  // stages is a power of two
+  int grid, stages, stage_shift, max_cov;  // stages: a multiple of the tile groups
   // queries
   const void* q;
   int qdt;
@@ -181,7 +182,7 @@ __device__ __forceinline__ void unit_codec_rows(const DecodeParams& p, const flo
 // BD = 0 is the generic path for block sizes other than 4 and 8.
 constexpr int kLutBlocks = 4;
 template <int R, int BD>
-__global__ void __launch_bounds__(kConsumers) lut_kernel(const __grid_constant__ DecodeParams p) {
+__global__ void __launch_bounds__(kLutThreads) lut_kernel(const __grid_constant__ DecodeParams p) {
   // only this unit's R query rows (keeps the CTA small enough to share an SM
   // with a decode CTA)
   __shared__ float qo[R][128], qc[R][128];
@@ -192,13 +193,13 @@ __global__ void __launch_bounds__(kConsumers) lut_kernel(const __grid_constant__
   const int rg = static_cast<int>(u - pair * p.n_rg);
   const int bb = static_cast<int>(pair / p.hkv), hh = static_cast<int>(pair % p.hkv);
   grid_launch_dependents();  // let the decode grid start streaming now
-  unit_query_rows(p, qo, rg, bb, hh, tid, kConsumers);
+  unit_query_rows(p, qo, rg, bb, hh, tid, kLutThreads);
   __syncthreads();
-  unit_codec_rows(p, qo, qc, tid, kConsumers);
+  unit_codec_rows(p, qo, qc, tid, kLutThreads);
   __syncthreads();
   float* out = p.lut_g + (size_t)u * (p.lut_unit_bytes / 4);
   if constexpr (BD > 0) {
-    const int b = b0 + tid / (kConsumers / kLutBlocks);
+    const int b = b0 + tid / (kLutThreads / kLutBlocks);
     if (b >= p.nb) return;
     const bool zero = p.n_heavy > 0 && p.heavy && p.heavy[b];
     float q[R][BD];
@@ -209,7 +210,7 @@ __global__ void __launch_bounds__(kConsumers) lut_kernel(const __grid_constant__
     const float* cb = p.cents + (size_t)b * p.k * BD;
     float* ob = out + (size_t)b * p.k * R;
 #pragma unroll 4
-    for (int c = tid % (kConsumers / kLutBlocks); c < p.k; c += kConsumers / kLutBlocks) {
+    for (int c = tid % (kLutThreads / kLutBlocks); c < p.k; c += kLutThreads / kLutBlocks) {
       float cv[BD];
 #pragma unroll
       for (int j = 0; j < BD; j += 4) {
@@ -236,7 +237,7 @@ __global__ void __launch_bounds__(kConsumers) lut_kernel(const __grid_constant__
     }
   } else {
     const int nbl = min(kLutBlocks, p.nb - b0);
-    for (int e = tid; e < nbl * p.k; e += kConsumers) {
+    for (int e = tid; e < nbl * p.k; e += kLutThreads) {
       const int b = b0 + e / p.k, c = e % p.k;
       const bool zero = p.n_heavy > 0 && p.heavy && p.heavy[b];
       const float* cv = p.cents + ((size_t)b * p.k + c) * p.bd;
@@ -251,8 +252,8 @@ __global__ void __launch_bounds__(kConsumers) lut_kernel(const __grid_constant__
   }
 }
 
-template <int R, int D, int NBC>
-__global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
+template <int R, int D, int NBC, int CW>
+__global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
     const __grid_constant__ DecodeParams p, const __grid_constant__ CUtensorMap map_v,
     const __grid_constant__ CUtensorMap map_vt) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -291,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
   __syncthreads();
 
   // ====================================================== producer warp
-  if (warp == kConsumerWarps) {
+  if (warp == CW) {
     if (lane == 0) {
       if (p.vfmt == SS_V_F16 && p.n_ct > 0) prefetch_tmap(&map_v);
       if (p.n_tt > 0 && p.vfmt == SS_V_F16) prefetch_tmap(&map_vt);
@@ -307,9 +308,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
           ++u;
           if (++rgc == p.n_rg) { rgc = 0; ++pair; }
         }
-        const int s = it & (p.stages - 1);
+        const int s = it % p.stages;
         if (it >= p.stages) {
-          if (ms.abort || !mbar_wait_bounded(&empty_bar[s], ((it >> p.stage_shift) - 1) & 1,
+          if (ms.abort || !mbar_wait_bounded(&empty_bar[s], ((it / p.stages) - 1) & 1,
                                              kWaitLimitNs)) {
             ms.abort = 1;
             atomicOr(p.err, 1);
@@ -370,8 +371,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
       const int issued = it;
       for (int j = issued - p.stages; j < issued; ++j) {
         if (j < 0) continue;
-        const int s = j & (p.stages - 1);
-        if (!mbar_wait_bounded(&full_bar[s], (j >> p.stage_shift) & 1, kWaitLimitNs)) {
+        const int s = j % p.stages;
+        if (!mbar_wait_bounded(&full_bar[s], (j / p.stages) & 1, kWaitLimitNs)) {
           atomicOr(p.err, 2);
           break;
         }
@@ -387,7 +388,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
   constexpr int TPL = slice_tokens(R) / 32;    // tokens per lane
   constexpr int SL = 32 * TPL;                 // tokens per warp slice
   const int wps = TILE / SL;                   // warps sharing one tile
-  const int tgroups = kConsumerWarps / wps;
+  const int tgroups = CW / wps;
   const int wgroup = warp / wps, slice = warp % wps;
   const int ctid = tid;                        // 0..255
   const int64_t q_off = p.tc + p.ttail - p.tq;
@@ -421,7 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
     // Tables are precomputed for all units by lut_kernel; one bulk copy brings
     // this unit's table into shared memory. Query rows are only needed here
     // for exact dot products (fp16 tail tokens, heavy blocks).
-    named_bar_sync(1, kConsumers);  // previous unit finalised, LUT region free
+    named_bar_sync(1, (CW * 32));  // previous unit finalised, LUT region free
     if (ctid == 0) {
       // Tables come from lut_kernel, launched just before as the primary of a
       // programmatic dependent launch: wait for its results once.
@@ -435,10 +436,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
                  bytes - off < 16384u ? bytes - off : 16384u, &lut_bar);
     }
     if (p.ttail > 0 || p.n_heavy > 0) {
-      unit_query_rows(p, ms.qo, rg, bb, hh, ctid, kConsumers);
-      named_bar_sync(1, kConsumers);
-      unit_codec_rows(p, ms.qo, ms.qc, ctid, kConsumers);
-      named_bar_sync(1, kConsumers);
+      unit_query_rows(p, ms.qo, rg, bb, hh, ctid, (CW * 32));
+      named_bar_sync(1, (CW * 32));
+      unit_codec_rows(p, ms.qo, ms.qc, ctid, (CW * 32));
+      named_bar_sync(1, (CW * 32));
     }
     if (!ms.abort && !mbar_wait_bounded(&lut_bar, unit_no & 1, kWaitLimitNs)) {
       ms.abort = 1;
@@ -466,8 +467,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
     for (int i = ifirst; i < n_here; i += tgroups) {
       const int it = it0 + i;
       const int lt = lt0 + i;
-      const int s = it & (p.stages - 1);
-      if (!ms.abort && !mbar_wait_bounded(&full_bar[s], (it >> p.stage_shift) & 1, kWaitLimitNs)) {
+      const int s = it % p.stages;
+      if (!ms.abort && !mbar_wait_bounded(&full_bar[s], (it / p.stages) & 1, kWaitLimitNs)) {
         ms.abort = 1;
         atomicOr(p.err, 4);
       }
@@ -757,10 +758,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
       for (int o = 1; o < 32; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
       l_w[r] = v;
     }
-    named_bar_sync(1, kConsumers);  // every warp is done with the LUT: reuse it as scratch
+    named_bar_sync(1, (CW * 32));  // every warp is done with the LUT: reuse it as scratch
     float* wo = lut;                                  // [8][R][D]
-    float* wm = lut + kConsumerWarps * R * D;         // [8][R]
-    float* wl = wm + kConsumerWarps * R;              // [8][R]
+    float* wm = lut + CW * R * D;         // [8][R]
+    float* wl = wm + CW * R;              // [8][R]
     {
       const int n0 = 2 * (lane & 3);
       const int m0 = lane >> 2;
@@ -781,13 +782,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
       }
     }
     if (ctid == 0) ms.is_last = 0;
-    named_bar_sync(1, kConsumers);
-    for (int e = ctid; e < R * D; e += kConsumers) {
+    named_bar_sync(1, (CW * 32));
+    for (int e = ctid; e < R * D; e += (CW * 32)) {
       const int r = e / D, j = e - r * D;
       float mstar = -INFINITY;
-      for (int w = 0; w < kConsumerWarps; ++w) mstar = fmaxf(mstar, wm[w * R + r]);
+      for (int w = 0; w < CW; ++w) mstar = fmaxf(mstar, wm[w * R + r]);
       float O = 0.f, L = 0.f;
-      for (int w = 0; w < kConsumerWarps; ++w) {
+      for (int w = 0; w < CW; ++w) {
         const float mg = wm[w * R + r];
         const float wt = (mg == -INFINITY) ? 0.f : exp2f((mg - mstar) * kLog2e);
         O = fmaf(wo[(w * R + r) * D + j], wt, O);
@@ -796,7 +797,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
       ms.o[r][j] = O;
       if (j == 0) { ms.mrow[r] = mstar; ms.lrow[r] = L; }
     }
-    named_bar_sync(1, kConsumers);
+    named_bar_sync(1, (CW * 32));
 
     // ---------------------------------------------- unit finalisation
     const int64_t first = cta_of(u * p.tpu, p.total_tiles, p.grid);
@@ -806,12 +807,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
     bool do_final = true;
     if (ncov > 1) {
       float* slot = p.slots + ((size_t)u * p.max_cov + (cta - first)) * R * row_floats;
-      for (int e = ctid; e < R * row_floats; e += kConsumers) {
+      for (int e = ctid; e < R * row_floats; e += (CW * 32)) {
         const int r = e / row_floats, j = e - r * row_floats;
         slot[e] = j < D ? ms.o[r][j] : (j == D ? ms.mrow[r] : ms.lrow[r]);
       }
       __threadfence();
-      named_bar_sync(1, kConsumers);
+      named_bar_sync(1, (CW * 32));
       if (ctid == 0) {
         const int prev = atomicAdd(p.counters + u, 1);
         if (prev == ncov - 1) {
@@ -819,12 +820,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
           p.counters[u] = 0;  // leave the counter ready for the next launch
         }
       }
-      named_bar_sync(1, kConsumers);
+      named_bar_sync(1, (CW * 32));
       do_final = ms.is_last != 0;
       if (do_final) {
         __threadfence();
         const float* base = p.slots + (size_t)u * p.max_cov * R * row_floats;
-        for (int e = ctid; e < R * D; e += kConsumers) {
+        for (int e = ctid; e < R * D; e += (CW * 32)) {
           const int r = e / D, j = e - r * D;
           float mstar = -INFINITY;
           for (int g = 0; g < ncov; ++g)
@@ -840,11 +841,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attn_kernel(
           ms.o[r][j] = O;
           if (j == 0) { ms.mrow[r] = mstar; ms.lrow[r] = L; }
         }
-        named_bar_sync(1, kConsumers);
+        named_bar_sync(1, (CW * 32));
       }
     }
     if (do_final) {
-      for (int e = ctid; e < R * D; e += kConsumers) {
+      for (int e = ctid; e < R * D; e += (CW * 32)) {
         const int r = e / D, j = e - r * D;
         const int rr = rg * R + r;
         if (rr >= rows_valid) continue;
@@ -909,7 +910,7 @@ __global__ void lse_merge_kernel(const float* parts, int n_parts, int64_t rows, 
 
 // ------------------------------------------------------------------ host plan
 struct Plan {
-  int R, tile, n_rg, n_ct, n_tt, tpu, grid, stages, max_cov, v_words, v_groups;
+  int R, cw, tile, n_rg, n_ct, n_tt, tpu, grid, stages, max_cov, v_words, v_groups;
   int64_t total_tiles, n_units;
   uint32_t stage_bytes, off_idx, off_aux, off_vdq, off_lut, off_p, off_misc;
   size_t smem;
@@ -918,7 +919,7 @@ struct Plan {
 
 constexpr size_t kSmemBudget = 226 * 1024;  // leaves room for static barriers
 
-int make_plan_r(const ss_decode_args* a, Plan& pl, int r_cap) {
+int make_plan_r(const ss_decode_args* a, Plan& pl, int r_cap, int cw) {
   SS_REQUIRE(a, "ss_decode_attn: null args");
   SS_REQUIRE(a->d == 64 || a->d == 128, "ss_decode_attn: head_dim must be 64 or 128");
   SS_REQUIRE(a->bd > 0 && a->bd <= 16 && a->d % a->bd == 0, "ss_decode_attn: bad block_dim");
@@ -975,24 +976,26 @@ int make_plan_r(const ss_decode_args* a, Plan& pl, int r_cap) {
   pl.stage_bytes = (pl.off_aux + aux + 1023) & ~1023u;
   size_t fixed = 0;
   // per-warp fp16 value slices (16 tokens) for the quantized path
-  const size_t vdq = (a->vfmt == SS_V_QUANT) ? (size_t)kConsumerWarps * 16 * a->d * 2 : 0;
+  const size_t vdq = (a->vfmt == SS_V_QUANT) ? (size_t)cw * 16 * a->d * 2 : 0;
   // the LUT region doubles as the per-warp merge scratch at unit ends
   size_t lut = (size_t)nb * a->k * R * 4;
-  const size_t scratch = (size_t)kConsumerWarps * R * (a->d + 2) * 4;
+  const size_t scratch = (size_t)cw * R * (a->d + 2) * 4;
   if (lut < scratch) lut = scratch;
-  const size_t pbytes = (size_t)kConsumerWarps * 64 * 16;
+  const size_t pbytes = (size_t)cw * 64 * 16;
   fixed = vdq + ((lut + 127) & ~size_t(127)) + pbytes + ((sizeof(Misc) + 127) & ~size_t(127)) + 1024;
   if (fixed + 2 * (size_t)pl.stage_bytes > kSmemBudget)
     return fail(SS_ERR_UNSUPPORTED, "ss_decode_attn: configuration exceeds shared memory");
   int stages = static_cast<int>((kSmemBudget - fixed) / pl.stage_bytes);
-  if (stages > 4) stages = 4;
+  if (stages > 6) stages = 6;
   // The consumer warps form tile groups that take tiles round robin; a warp may
   // only wait for the barrier phase right after the one it consumed last,
   // which holds when the stage count is a multiple of the number of groups.
-  const int tgroups = slice_tokens(R) / 16;  // = consumer warps / warps per tile
+  const int tgroups = cw * slice_tokens(R) / static_cast<int>(T);  // warps / warps per tile
   stages -= stages % tgroups;
-  if (stages < tgroups)
+  // 12 consumer warps only pay off with two free stages beyond the three in use
+  if (stages < tgroups || (cw > 8 && stages < tgroups + 2))
     return fail(SS_ERR_UNSUPPORTED, "ss_decode_attn: configuration exceeds shared memory");
+  pl.cw = cw;
   pl.stages = stages;
   size_t off = (size_t)stages * pl.stage_bytes;
   pl.off_vdq = static_cast<uint32_t>(off);
@@ -1017,15 +1020,23 @@ int make_plan_r(const ss_decode_args* a, Plan& pl, int r_cap) {
 // Largest row group that fits: 8 query rows per unit need a 128 KB table next
 // to the stage ring; when that does not fit (wide stages, e.g. heavy key
 // blocks) the rows are split into groups of 4, which streams the unit twice.
+// 12 consumer warps (more latency hiding for the table gather) when six
+// stages fit, i.e. for compact value formats; 8 warps with 4 stages otherwise.
 int make_plan(const ss_decode_args* a, Plan& pl) {
-  int rc = make_plan_r(a, pl, 8);
-  if (rc == SS_ERR_UNSUPPORTED && pl.R == 8) rc = make_plan_r(a, pl, 4);
+  int rc = SS_ERR_UNSUPPORTED;
+  for (int r_cap : {8, 4}) {
+    for (int cw : {12, 8}) {
+      rc = make_plan_r(a, pl, r_cap, cw);
+      if (rc != SS_ERR_UNSUPPORTED) return rc;
+    }
+    if (pl.R != 8) break;  // a smaller row group cannot help
+  }
   return rc;
 }
 
 template <int R, int D>
 int launch_decode(const DecodeParams& p, const CUtensorMap& mv, const CUtensorMap& mvt,
-                  size_t smem, cudaStream_t st) {
+                  size_t smem, int cw, cudaStream_t st) {
   const dim3 lgrid(static_cast<unsigned>(p.n_units), (p.nb + kLutBlocks - 1) / kLutBlocks);
   // Same shared-memory carveout as the decode kernel: no reconfiguration
   // between the two launches of every step.
@@ -1036,20 +1047,21 @@ int launch_decode(const DecodeParams& p, const CUtensorMap& mv, const CUtensorMa
     cudaFuncSetAttribute(lut_kernel<R, 0>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     carveout_set = true;
   }
-  if (p.bd == 8) lut_kernel<R, 8><<<lgrid, kConsumers, 0, st>>>(p);
-  else if (p.bd == 4) lut_kernel<R, 4><<<lgrid, kConsumers, 0, st>>>(p);
-  else lut_kernel<R, 0><<<lgrid, kConsumers, 0, st>>>(p);
+  if (p.bd == 8) lut_kernel<R, 8><<<lgrid, kLutThreads, 0, st>>>(p);
+  else if (p.bd == 4) lut_kernel<R, 4><<<lgrid, kLutThreads, 0, st>>>(p);
+  else lut_kernel<R, 0><<<lgrid, kLutThreads, 0, st>>>(p);
   int rc = check_launch("ss_decode_attn (tables)");
   if (rc != SS_OK) return rc;
-  auto kern = (p.nb == 16 && p.k == 256) ? decode_attn_kernel<R, D, 16>
-                                         : decode_attn_kernel<R, D, 0>;
+  const bool nb16 = p.nb == 16 && p.k == 256;
+  auto kern = cw == 12 ? (nb16 ? decode_attn_kernel<R, D, 16, 12> : decode_attn_kernel<R, D, 0, 12>)
+                       : (nb16 ? decode_attn_kernel<R, D, 16, 8> : decode_attn_kernel<R, D, 0, 8>);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess)
     return fail(SS_ERR_CUDA, std::string("ss_decode_attn: smem attribute: ") + cudaGetErrorString(e));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.grid);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(cw * 32 + 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -1155,7 +1167,7 @@ int run_decode(const ss_decode_args* a, float* part_out, void* stream) {
   p.off_stage = 0;
   count_dispatch(part_out ? "ss_decode_attn_partial" : "ss_decode_attn");
 #define SS_DISPATCH(RV, DV) \
-  if (pl.R == RV && a->d == DV) return launch_decode<RV, DV>(p, mv, mvt, pl.smem, st);
+  if (pl.R == RV && a->d == DV) return launch_decode<RV, DV>(p, mv, mvt, pl.smem, pl.cw, st);
   SS_DISPATCH(1, 128) SS_DISPATCH(2, 128) SS_DISPATCH(4, 128) SS_DISPATCH(8, 128)
   SS_DISPATCH(1, 64) SS_DISPATCH(2, 64) SS_DISPATCH(4, 64) SS_DISPATCH(8, 64)
 #undef SS_DISPATCH
