@@ -17,6 +17,7 @@ import torch
 
 from . import _lib as L
 from . import kernels as K
+from .cache import SunShapeKVCache
 
 __all__ = ["sunshape_sdpa", "decode_partials", "workspace_for", "PreparedDecode"]
 
@@ -176,6 +177,8 @@ def sunshape_sdpa(queries, cache, scale: float, mask=None) -> torch.Tensor:
     tkv = cache.offset
     if tkv == 0:
         return torch.zeros_like(q)
+    if mask is None and isinstance(cache, SunShapeKVCache):
+        return _sdpa_simple_fast(q, cache, scale)
     codec = cache.codec
     spec = cache.attention_spec()
     m, mode, causal = _prepare_mask(mask, Tq, tkv, q.device)
@@ -186,6 +189,43 @@ def sunshape_sdpa(queries, cache, scale: float, mask=None) -> torch.Tensor:
     n_heavy = codec.n_heavy_blocks if spec.get("kheavy") is not None else 0
     _run_decode(q, centroids=codec.centroids, perm=perm, scale=scale, spec=spec, causal=causal,
                 out=out, mask=m, rot_k=rot_k, heavy=codec.heavy_u8, n_heavy=n_heavy)
+    codec.last_score_backend = "cuda_fused"
+    return out
+
+
+def _sdpa_simple_fast(q: torch.Tensor, cache, scale: float) -> torch.Tensor:
+    """sunshape_sdpa for the simple cache without a mask: the argument block
+    is kept on the cache and rebuilt only when the storage is reallocated or
+    the query layout, dtype or scale changes; per call only the query and
+    output pointers and the token count are updated."""
+    codec = cache.codec
+    key = (cache._epoch, tuple(q.shape), tuple(q.stride()), q.dtype, float(scale),
+           codec.centroids.data_ptr(), codec.permutation.data_ptr(), codec.use_rotation)
+    memo = cache._sdpa_memo
+    if memo is None or memo[0] != key:
+        spec = cache.attention_spec()
+        perm = codec.permutation if codec._is_perm() else None
+        rot_k = codec.rotation.contiguous() if codec.use_rotation else None
+        n_heavy = codec.n_heavy_blocks if spec.get("kheavy") is not None else 0
+        out = torch.empty_like(q)
+        a, keep = _fill_args(q, codec.centroids, perm, scale, spec, False, out, None, rot_k,
+                             codec.heavy_u8, n_heavy)
+        keep += [spec, rot_k]
+        lib = L.load()
+        memo = (key, a, keep, lib, C.byref(a))
+        cache._sdpa_memo = memo
+    _, a, _, lib, ref = memo
+    out = torch.empty_like(q)
+    a.q = q.data_ptr()
+    a.out = out.data_ptr()
+    a.tc = cache.offset
+    nbytes = lib.ss_decode_workspace_size(ref)
+    if nbytes == 0:
+        raise L.SunShapeCudaError("ss_decode_workspace_size", 1, L.last_error())
+    ws = workspace_for(q.device, nbytes)
+    a.workspace = ws.data_ptr()
+    a.workspace_bytes = ws.numel()
+    L.check("ss_decode_attn", lib.ss_decode_attn(ref, L.stream_ptr(q.device)))
     codec.last_score_backend = "cuda_fused"
     return out
 

@@ -72,6 +72,9 @@ class SunShapeKVCache:
         self._values = None
         self._capacity = 0
         self._batch = 0
+        self._epoch = 0          # bumped whenever the storage is reallocated
+        self._assign_memo = None
+        self._sdpa_memo = None
 
     # ------------------------------------------------------------ storage
     def _ensure_capacity(self, B: int, new_tokens: int) -> None:
@@ -81,6 +84,7 @@ class SunShapeKVCache:
             raise ValueError(f"batch size changed from {self._batch} to {B}")
         if need <= self._capacity:
             return
+        self._epoch += 1
         cap = _round_up(need, _STEP)
         H, dev = self.n_kv_heads, self.device
         self._key_indices = _grow(self._key_indices, (B, H, cap, self.n_blocks), self.offset,
@@ -108,10 +112,42 @@ class SunShapeKVCache:
             return
         self._ensure_capacity(B, T)
         o = self.offset
-        _quantize_keys_into(self.codec, k, self._key_indices[:, :, o:o + T],
-                            None if self._key_heavy is None else self._key_heavy[:, :, o:o + T])
-        self._values[:, :, o:o + T] = v
+        if not self._assign_fast(k, o):
+            _quantize_keys_into(self.codec, k, self._key_indices[:, :, o:o + T],
+                                None if self._key_heavy is None else self._key_heavy[:, :, o:o + T])
+        self._values.narrow(2, o, T).copy_(v)
         self.offset += T
+
+    def _assign_fast(self, k: torch.Tensor, o: int) -> bool:
+        """ss_vq_assign straight into the index stream at token o, with the
+        arguments that only change on reallocation kept from the last call
+        (the per-token decode append is otherwise dominated by host work)."""
+        codec = self.codec
+        B, H, T, D = k.shape
+        if codec.use_rotation or k.stride(3) != 1 or k.stride(0) != H * k.stride(1):
+            return False
+        key = (self._epoch, k.dtype, k.stride(1), k.stride(2), codec.centroids.data_ptr(),
+               codec.permutation.data_ptr(), codec._is_perm(), codec.n_heavy_blocks)
+        memo = self._assign_memo
+        if memo is None or memo[0] != key:
+            L = K.L
+            perm = codec.permutation if codec._is_perm() else None
+            ki, kh = self._key_indices, self._key_heavy
+            memo = (key, L.load().ss_vq_assign, L.dtype_code(k.dtype), B * H, k.stride(1),
+                    k.stride(2), D, L.ptr(perm), L.ptr(codec.centroids), codec.block_dim,
+                    codec.n_centroids, L.ptr(codec.heavy_u8), ki.data_ptr(), ki.stride(1),
+                    ki.stride(2), None if kh is None else kh.data_ptr(),
+                    0 if kh is None else kh.stride(1), 0 if kh is None else kh.stride(2),
+                    codec)
+            self._assign_memo = memo
+        (_, fn, dt, g, kgs, krs, d, perm_p, cents_p, bd, kc, heavy_p, ki_p, igs, irs, kh_p, hgs,
+         hrs, _) = memo
+        rc = fn(K.L.C.c_void_p(k.data_ptr()), dt, g, T, kgs, krs, d, perm_p, cents_p, bd, kc,
+                heavy_p, K.L.C.c_void_p(ki_p + o * irs), igs, irs,
+                None if kh_p is None else K.L.C.c_void_p(kh_p + 2 * o * hrs), hgs, hrs, None, 0,
+                K.L.stream_ptr(self.device))
+        K.L.check("ss_vq_assign", rc)
+        return True
 
     def update_and_fetch(self, keys, values):
         """cache.py:156-205: append, then return (keys, values) as stored

@@ -146,6 +146,75 @@ __global__ void __launch_bounds__(kAssignThreads) vq_assign_kernel(AssignParams 
   }
 }
 
+// Few rows (a decode step's append): one CTA per (32-row tile, block); warp w
+// scores centroids [w*k/16, (w+1)*k/16) for the tile's rows (lane = row), and
+// the 16 partial winners are reduced in warp order. Same result as the
+// sequential reference loop: the first index whose distance is below all
+// earlier ones, a NaN distance at index 0 keeps 0.
+template <int BD>
+__global__ void __launch_bounds__(kAssignThreads) vq_assign_small_kernel(AssignParams p) {
+  __shared__ float s_best[16][32];
+  __shared__ int s_bi[16][32];
+  __shared__ float s_d0[32];
+  const int b = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t n_rows = p.n_groups * p.rpg;
+  const int64_t r = (int64_t)blockIdx.x * kAssignRows + lane;
+  const bool valid = r < n_rows;
+  int64_t g = 0, t = 0;
+  if (valid) { g = r / p.rpg; t = r - g * p.rpg; }
+  float kk[BD];
+#pragma unroll
+  for (int j = 0; j < BD; ++j) {
+    const int col = b * BD + j;
+    kk[j] = valid ? load_as_f32(p.keys, p.key_dtype, g * p.kgs + t * p.krs + (p.perm ? p.perm[col] : col))
+                  : 0.f;
+  }
+  const bool heavy = p.heavy && p.heavy[b];
+  if (heavy) {
+    if (warp == 0 && valid) {
+      if (p.out_heavy) {
+        int hpos = 0;
+        for (int bb = 0; bb < b; ++bb) hpos += p.heavy[bb] ? 1 : 0;
+        uint16_t* dst = p.out_heavy + g * p.hgs + t * p.hrs + hpos * BD;
+#pragma unroll
+        for (int j = 0; j < BD; ++j) dst[j] = f2h(kk[j]);
+      }
+      if (p.out_pt) {
+        float* dst = p.out_pt + r * (int64_t)p.nb * BD + b * BD;
+#pragma unroll
+        for (int j = 0; j < BD; ++j) dst[j] = kk[j];
+      }
+      p.out_idx[g * p.igs + t * p.irs + b] = 0;
+    }
+    return;
+  }
+  const float* cb = p.cents + (size_t)b * p.k * BD;
+  const int per = (p.k + 15) / 16;
+  const int c0 = warp * per, c1 = min(p.k, c0 + per);
+  float best = __int_as_float(0x7f800000);
+  int bi = 0x7fffffff;
+  for (int c = c0; c < c1; ++c) {
+    const float* cc = cb + (size_t)c * BD;
+    const float dd = p.dist_mode == 0 ? dist_direct<BD>(kk, cc) : dist_expanded<BD>(kk, cc);
+    if (c == 0) s_d0[lane] = dd;
+    if (dd < best) { best = dd; bi = c; }
+  }
+  s_best[warp][lane] = best;
+  s_bi[warp][lane] = bi;
+  __syncthreads();
+  if (warp == 0 && valid) {
+    float bv = s_best[0][lane];
+    int bx = s_bi[0][lane];
+    for (int w = 1; w < 16; ++w) {
+      if (s_best[w][lane] < bv) { bv = s_best[w][lane]; bx = s_bi[w][lane]; }
+    }
+    const float d0 = s_d0[lane];
+    const int idx = (d0 != d0 || bx == 0x7fffffff) ? 0 : bx;
+    p.out_idx[g * p.igs + t * p.irs + b] = static_cast<uint8_t>(idx);
+  }
+}
+
 // ------------------------------------------------------------------ k-means
 // One thread per (block, centroid): scans all rows in order and accumulates
 // the assigned ones with float32 adds (same order as np.add.at).
@@ -321,6 +390,8 @@ namespace {
 int g_assign_path = 0;
 // Below this many rows the CUDA-core kernel has the lower latency.
 constexpr int64_t kTcMinRows = 16384;
+// At most this many rows: the (row tile x block) kernel for small appends.
+constexpr int64_t kSmallRows = 4096;
 }  // namespace
 
 extern "C" {
@@ -362,6 +433,20 @@ int ss_vq_assign(const void* keys, int key_dtype, int64_t n_groups, int64_t rows
                  d, d / bd, k, perm, centroids, heavy, out_idx, idx_group_stride,
                  idx_row_stride, out_heavy, heavy_group_stride, heavy_row_stride, out_pt,
                  dist_mode, 0};
+  if (n_groups * rows_per_group <= kSmallRows && g_assign_path != 2) {
+    // a decode step's append: spread (row tile, block) pairs over the SMs
+    const dim3 grid_s(static_cast<unsigned>((n_groups * rows_per_group + kAssignRows - 1) / kAssignRows),
+                      static_cast<unsigned>(p.nb));
+    cudaStream_t sst = as_stream(stream);
+    switch (bd) {
+      case 2: vq_assign_small_kernel<2><<<grid_s, kAssignThreads, 0, sst>>>(p); break;
+      case 4: vq_assign_small_kernel<4><<<grid_s, kAssignThreads, 0, sst>>>(p); break;
+      case 8: vq_assign_small_kernel<8><<<grid_s, kAssignThreads, 0, sst>>>(p); break;
+      case 16: vq_assign_small_kernel<16><<<grid_s, kAssignThreads, 0, sst>>>(p); break;
+      default: return fail(SS_ERR_UNSUPPORTED, "ss_vq_assign: block_dim must be 2, 4, 8 or 16");
+    }
+    return check_launch("ss_vq_assign (small)");
+  }
   // Blocks per CTA so that the centroid slice stays within ~160 KB of smem.
   const size_t per_block = (size_t)k * bd * 4 + (size_t)k * 4;
   int bpc = static_cast<int>((160 * 1024) / per_block);
