@@ -102,6 +102,17 @@ struct DecodeParams {
 // gives two tile groups of four warps, so four stages double-buffer each group.
 __host__ __device__ constexpr int slice_tokens(int) { return 32; }
 
+__device__ __forceinline__ uint32_t pack_halves2(__half lo, __half hi) {
+  return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
+}
+
+// Maximum of v over the warp (NaN inputs ignored, as fmaxf does).
+__device__ __forceinline__ float warp_max_f32(float v) {
+  float r;
+  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+  return r;
+}
+
 // 2^x with the SFU approximation (ex2.approx.ftz): |rel err| < 2^-22.
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
@@ -604,11 +615,10 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
 
       // 2. online softmax over this warp's slice
       float alpha[R];
+      __half ph0[R], ph1[R];
 #pragma unroll
       for (int r = 0; r < R; ++r) {
-        float mx = TPL > 1 ? fmaxf(s0[r], s1[r]) : s0[r];
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const float mx = warp_max_f32(TPL > 1 ? fmaxf(s0[r], s1[r]) : s0[r]);
         const float mn = fmaxf(m_w[r], mx);
         float p0 = 0.f, p1 = 0.f;
         if (mn == -INFINITY) {
@@ -619,12 +629,34 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
           p1 = fast_exp2((s1[r] - mn) * kLog2e);
         }
         const __half h0 = __float2half_rn(p0), h1 = __float2half_rn(p1);
-        Pw[lane * 8 + r] = h0;
-        if (TPL > 1) Pw[(lane + 32) * 8 + r] = h1;
+        ph0[r] = h0;
+        ph1[r] = h1;
         l_l[r] = l_l[r] * alpha[r] + (__half2float(h0) + (TPL > 1 ? __half2float(h1) : 0.f));
         m_w[r] = mn;
       }
-      {
+      // this lane's weights for all rows in one store per token
+      if constexpr (R == 4 || R == 8) {
+#pragma unroll
+        for (int r4 = 0; r4 < R; r4 += 4) {
+          *reinterpret_cast<uint2*>(Pw + lane * 8 + r4) =
+              make_uint2(pack_halves2(ph0[r4], ph0[r4 + 1]), pack_halves2(ph0[r4 + 2], ph0[r4 + 3]));
+          if (TPL > 1)
+            *reinterpret_cast<uint2*>(Pw + (lane + 32) * 8 + r4) =
+                make_uint2(pack_halves2(ph1[r4], ph1[r4 + 1]), pack_halves2(ph1[r4 + 2], ph1[r4 + 3]));
+        }
+      } else {
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          Pw[lane * 8 + r] = ph0[r];
+          if (TPL > 1) Pw[(lane + 32) * 8 + r] = ph1[r];
+        }
+      }
+      // The running maxima rarely move after the first tiles: rescale the
+      // accumulators only when one did (alpha is uniform across the warp).
+      bool moved = false;
+#pragma unroll
+      for (int r = 0; r < R; ++r) moved = moved || alpha[r] != 1.f;
+      if (moved) {
         const int n0 = 2 * (lane & 3);
         float a0 = 1.f, a1 = 1.f;
 #pragma unroll
