@@ -313,16 +313,16 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
       int lt = static_cast<int>(t_begin - u * p.tpu);
       int64_t pair = u / p.n_rg;
       int rgc = static_cast<int>(u - pair * p.n_rg);
+      int s = 0, ph = 0;  // stage of tile `it` and its use count parity
       for (int64_t tau = t_begin; tau < t_end; ++tau, ++it) {
         if (tau != t_begin && ++lt == p.tpu) {
           lt = 0;
           ++u;
           if (++rgc == p.n_rg) { rgc = 0; ++pair; }
         }
-        const int s = it % p.stages;
+        if (it > 0 && ++s == p.stages) { s = 0; ph ^= 1; }
         if (it >= p.stages) {
-          if (ms.abort || !mbar_wait_bounded(&empty_bar[s], ((it / p.stages) - 1) & 1,
-                                             kWaitLimitNs)) {
+          if (ms.abort || !mbar_wait_bounded(&empty_bar[s], ph ^ 1, kWaitLimitNs)) {
             ms.abort = 1;
             atomicOr(p.err, 1);
             break;
@@ -475,11 +475,16 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
     const int lt0 = static_cast<int>(tau - u * p.tpu);
     const int n_here = static_cast<int>(u_end - tau);
     const int ifirst = (wgroup - it0 % tgroups + tgroups) % tgroups;
+    // stage and phase of this warp's first tile; later tiles advance by the
+    // number of tile groups, which divides the stage count
+    int s = (it0 + ifirst) % p.stages, ph = ((it0 + ifirst) / p.stages) & 1;
     for (int i = ifirst; i < n_here; i += tgroups) {
-      const int it = it0 + i;
+      if (i != ifirst) {
+        s += tgroups;
+        if (s >= p.stages) { s -= p.stages; ph ^= 1; }
+      }
       const int lt = lt0 + i;
-      const int s = it % p.stages;
-      if (!ms.abort && !mbar_wait_bounded(&full_bar[s], (it / p.stages) & 1, kWaitLimitNs)) {
+      if (!ms.abort && !mbar_wait_bounded(&full_bar[s], ph, kWaitLimitNs)) {
         ms.abort = 1;
         atomicOr(p.err, 4);
       }
