@@ -569,6 +569,80 @@ def run_assign(args):
     }
 
 
+# ---------------------------------------------------------------------- value encode (cache fill)
+def run_encode(args):
+    """Value encoders on the config-3 value stream: 64 x 8 kv-heads x 8192
+    fp16 tokens (1 GiB) per step, encoded into cache-layout buffers."""
+    import torch
+    from sunshape_mlx_b200.value_codecs import GroupedValueCodec, TurboQuantValueCodec
+    import oracle as O
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    Bv, Tv = 64, 8192
+    g = torch.Generator(device=device).manual_seed(41)
+    v = torch.randn((Bv * HKV, Tv, D), generator=g, device=device).half()
+    n_th = Bv * HKV * Tv
+    fmts = {
+        "tq2_g32_fp16": TurboQuantValueCodec(head_dim=D, bits=2, group_size=32, device=device),
+        "tq2_reference": TurboQuantValueCodec(head_dim=D, bits=2, device=device),
+        "grouped2_g64": GroupedValueCodec(head_dim=D, bits=2, group_size=64),
+        "grouped4_g64": GroupedValueCodec(head_dim=D, bits=4, group_size=64),
+    }
+    peak, peak_kind = _peaks()
+    res = {}
+    for name, vc in fmts.items():
+        packed = torch.empty((Bv * HKV, Tv, vc.packed_dim), dtype=torch.int32, device=device)
+        if isinstance(vc, TurboQuantValueCodec):
+            sc = (torch.empty((Bv * HKV, Tv), dtype=torch.float32, device=device) if vc.group_size is None
+                  else torch.empty((Bv * HKV, Tv, vc.n_scale_groups), dtype=torch.float16, device=device))
+            step = lambda: vc.quantize_into(v, packed, sc)
+            out_b = vc.packed_dim * 4 + (4 if vc.group_size is None else 2 * vc.n_scale_groups)
+        else:
+            sc = torch.empty((Bv * HKV, Tv, vc.n_groups), dtype=torch.float32, device=device)
+            zr = torch.empty_like(sc)
+            step = lambda: vc.quantize_into(v, packed, sc, zr)
+            out_b = vc.packed_dim * 4 + 8 * vc.n_groups
+        for _ in range(max(3, args.warmup)):
+            step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        alg = n_th * (2 * D + out_b)
+        res[name] = {"ms_per_step": ms, "token_heads_per_s": n_th / (ms / 1e3),
+                     "bytes_per_token_head": 2 * D + out_b, "achieved_gbs": alg / (ms / 1e3) / 1e9,
+                     "frac": alg / (ms / 1e3) / 1e9 / peak}
+    main = res["tq2_g32_fp16"]
+    # CPU baseline: the oracle's grouped TurboQuant encode on 8192 rows
+    rot = fmts["tq2_g32_fp16"].rotation.cpu().numpy()
+    sample = v[0].float().cpu().numpy()
+    t0 = time.perf_counter()
+    O.tq_group_quantize(sample, rot, 2, 32)
+    cpu_v = sample.shape[0] / (time.perf_counter() - t0)
+    return {
+        "metric": "value encode (cache fill) token-heads/s", "value": main["token_heads_per_s"],
+        "unit": "token-heads/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": main["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16 in, 2-bit codes + fp16 scales out",
+        "data": "synthetic (N(0,1) fp16 values)",
+        "config": {"workload": "cfg3 value stream: 64 x 8 kv-heads x 8192 tokens, head_dim 128, "
+                               "TurboQuant-style 2-bit, rotated, fp16 scale per 32 channels",
+                   "l2": "inputs larger than L2 (1 GiB of values per step)"},
+        "roofline": {"bound": "hbm", "achieved": main["achieved_gbs"], "peak": peak, "unit": "GB/s",
+                     "frac": main["frac"], "peak_source": peak_kind},
+        "variants": res,
+        "gpu_launches": args.steps,
+        "cpu_baseline": {"value": cpu_v, "unit": "token-heads/s", "cores": os.cpu_count(),
+                         "kind": "port", "sample": "8192 rows through the oracle's grouped "
+                                                   "TurboQuant encode (NumPy)"},
+    }
+
+
 # ---------------------------------------------------------------------- reference arm
 def run_reference(args):
     """The reference's CPU path (oracle port of its NumPy quantize loop and
@@ -621,6 +695,8 @@ def main():
     ap.add_argument("--assign", action="store_true",
                     help="benchmark the cache-fill quantize (ss_vq_assign) instead of decode")
     ap.add_argument("--assign-path", choices=["tensor", "simt", "auto"], default="tensor")
+    ap.add_argument("--encode", action="store_true",
+                    help="benchmark the value encoders (config-3 value stream)")
     ap.add_argument("--profile", action="store_true",
                     help="build the workload, run warmup+steps decode launches, exit "
                          "(short command for ncu captures)")
@@ -635,6 +711,9 @@ def main():
     import torch
     import torch.distributed as dist
 
+    if args.encode:
+        print(json.dumps(run_encode(args)), flush=True)
+        return
     if args.assign:
         line = run_assign(args)
         if line is not None:

@@ -20,7 +20,8 @@ from .rotation import (
     safe_normalize,
 )
 from .codec import SunShapeBlockCodec, SunShapeQuantized
-from .cache import HybridSunShapeKVCache, SunShapeKVCache, create_kv_cache
+from .cache import (HybridSunShapeKVCache, SunShapeKVCache, create_kv_cache, load_cache,
+                    save_cache)
 from .attention import sunshape_sdpa
 from .kernels import (
     block_vq_quantize_metal,
@@ -51,4 +52,5 @@ __all__ = [
     "fused_attention_causal_metal", "fused_attention_dequant_metal",
     "fused_attention_dequant_causal_metal", "block_vq_quantize_metal", "GroupedValueCodec",
     "TurboQuantValueCodec", "create_kv_cache", "get_kernel_stats", "reset_kernel_stats",
+    "save_cache", "load_cache",
 ]

@@ -21,7 +21,8 @@ from . import kernels as K
 from .codec import SunShapeBlockCodec
 from .value_codecs import GroupedValueCodec, TurboQuantValueCodec, build_value_codec
 
-__all__ = ["SunShapeKVCache", "HybridSunShapeKVCache", "create_kv_cache"]
+__all__ = ["SunShapeKVCache", "HybridSunShapeKVCache", "create_kv_cache", "save_cache",
+           "load_cache"]
 
 _STEP = 256
 _DEFAULT_BUFFER_SIZE = 128
@@ -649,3 +650,91 @@ def create_kv_cache(codec: SunShapeBlockCodec, *, n_kv_heads: int = 1, head_dim:
         value_backend=value_backend, value_bits=value_bits, value_group_size=value_group_size,
         value_seed=value_seed, value_codec=value_codec, prefer_metal_kernels=prefer_metal_kernels,
         tq_group_size=tq_group_size, value_rotation=value_rotation)
+
+
+# ---------------------------------------------------------------- serialization
+# The reference only exposes the raw arrays (`state`, cache.py:256-262,
+# 988-998); these save and restore a cache completely (codec, value codec,
+# every stream and the offsets), so a prompt cache can be stored and decoding
+# resumed from it with identical results.
+_DTYPES = {str(d): d for d in (torch.float16, torch.bfloat16, torch.float32)}
+
+
+def _codec_from_state(st: dict, device) -> SunShapeBlockCodec:
+    c = SunShapeBlockCodec(head_dim=int(st["head_dim"]), block_dim=int(st["block_dim"]),
+                           n_centroids=int(st["n_centroids"]), mode=str(st["mode"]),
+                           device=device)
+    return c.load_state_dict(st)
+
+
+def _cache_state(cache) -> dict:
+    fields = {}
+    for name, val in vars(cache).items():
+        if name.endswith("_memo") or name in ("codec", "value_codec", "_value_codec_impl", "device"):
+            continue
+        if isinstance(val, torch.Tensor):
+            fields[name] = val.detach().cpu()
+        elif isinstance(val, torch.dtype):
+            fields[name] = str(val)
+        elif val is None or isinstance(val, (bool, int, float, str)):
+            fields[name] = val
+    st = {"kind": type(cache).__name__, "codec": cache.codec.state_dict(), "fields": fields}
+    vc = getattr(cache, "value_codec", None)
+    if vc is not None and vc is not cache.codec:
+        st["value_codec"] = vc.state_dict()
+    impl = getattr(cache, "_value_codec_impl", None)
+    if impl is not None and getattr(impl, "rotation", None) is not None:
+        st["value_rotation"] = impl.rotation.detach().cpu()
+        st["tq_group_size"] = getattr(impl, "group_size", None)
+    return st
+
+
+def _restore_fields(cache, fields: dict) -> None:
+    for name, val in fields.items():
+        if isinstance(val, torch.Tensor):
+            val = val.to(cache.device)
+        elif name == "dtype" or (isinstance(val, str) and val in _DTYPES and name.endswith("dtype")):
+            val = _DTYPES.get(val, val)
+        setattr(cache, name, val)
+    if hasattr(cache, "_epoch"):
+        cache._epoch += 1  # cached launch arguments refer to the old storage
+
+
+def cache_state_dict(cache) -> dict:
+    """CPU-tensor state of a SunShape cache (simple or hybrid), codec included."""
+    return _cache_state(cache)
+
+
+def cache_from_state_dict(st: dict, device=None, codec: SunShapeBlockCodec | None = None):
+    """Rebuilds a cache saved by :func:`cache_state_dict` on `device`."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    codec = codec or _codec_from_state(st["codec"], dev)
+    f = st["fields"]
+    dtype = _DTYPES.get(f.get("dtype"), torch.float16)
+    if st["kind"] == "SunShapeKVCache":
+        cache = SunShapeKVCache(codec, n_kv_heads=int(f["n_kv_heads"]),
+                                head_dim=int(f["head_dim"]), dtype=dtype)
+    elif st["kind"] == "HybridSunShapeKVCache":
+        vcodec = _codec_from_state(st["value_codec"], dev) if "value_codec" in st else None
+        cache = HybridSunShapeKVCache(
+            codec, n_kv_heads=int(f["n_kv_heads"]), head_dim=int(f["head_dim"]), dtype=dtype,
+            buffer_size=int(f["buffer_size"]), value_backend=f["value_backend"],
+            value_bits=f["value_bits"], value_group_size=int(f["value_group_size"]),
+            value_seed=int(f["value_seed"]), value_codec=vcodec,
+            tq_group_size=st.get("tq_group_size"), value_rotation=st.get("value_rotation"))
+    else:
+        raise ValueError(f"unknown cache kind {st['kind']!r}")
+    _restore_fields(cache, f)
+    return cache
+
+
+def save_cache(cache, path) -> None:
+    """Writes a cache (and its codecs) to `path` (torch.save of CPU tensors)."""
+    torch.save(cache_state_dict(cache), path)
+
+
+def load_cache(path, device=None, codec: SunShapeBlockCodec | None = None):
+    """Loads a cache written by :func:`save_cache`; decoding continues from it."""
+    return cache_from_state_dict(torch.load(path, map_location="cpu", weights_only=False),
+                                 device=device, codec=codec)
+
