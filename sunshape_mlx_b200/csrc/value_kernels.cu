@@ -180,6 +180,204 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32)
   }
 }
 
+// TurboQuant encode on tensor cores (fp16 values, D = 128, 2 or 4 bits): the
+// rotation r = v R^T is an M=16-row x N=128 x K=128 warp MMA chain per 16 rows
+// with the rotation split into fp16 hi + lo (fp32 accumulate, about fp32
+// accuracy; the reference's own summation order is unspecified BLAS). Rows
+// are staged by 16-byte loads; norms / group scales, thresholds and code
+// packing run on the accumulator fragments (lane (g, t) holds rows g, g + 8
+// and columns 8 n + 2t, 2t + 1 of every 8-column tile n).
+constexpr int kTqWarps = 16;
+constexpr int kTqStride = 136;  // halves per staged row (128 + 8: conflict-free ldmatrix)
+
+template <int BITS>
+__global__ void __launch_bounds__(kTqWarps * 32)
+    encode_tq_mma_kernel(const __half* v, RowAddr ra, int64_t vgs, int64_t vrs, int mode, const float* rot, const float* bnd, uint32_t* packed,
+                         int64_t pgs, int64_t prs, void* scales, int64_t sgs, int64_t srs) {
+  extern __shared__ __align__(16) __half sm_tq[];
+  __half* s_rh = sm_tq;                          // [128][kTqStride] rotation, hi
+  __half* s_rl = s_rh + 128 * kTqStride;         // [128][kTqStride] rotation, lo
+  __half* s_rows = s_rl + 128 * kTqStride;       // [warps][2 buffers][16][kTqStride]
+  __shared__ float s_b[16];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  constexpr int nbnd = (1 << BITS) - 1;
+  constexpr int bits = BITS;
+  for (int e = threadIdx.x; e < 128 * 128; e += blockDim.x) {
+    const int i = e >> 7, j = e & 127;
+    const float x = rot[e];
+    const __half h = __float2half_rn(x);
+    s_rh[i * kTqStride + j] = h;
+    s_rl[i * kTqStride + j] = __float2half_rn(x - __half2float(h));
+  }
+  if (threadIdx.x < nbnd) s_b[threadIdx.x] = bnd[threadIdx.x];
+  __syncthreads();
+  __half* rows2 = s_rows + warp * 2 * 16 * kTqStride;
+  const uint32_t a_off =
+      (((lane & 7) + ((lane >> 3) & 1) * 8) * kTqStride + ((lane >> 4) & 1) * 8) * 2;
+  const uint32_t bh_base = smem_u32(s_rh) +
+                           (((lane & 7) + ((lane >> 4) & 1) * 8) * kTqStride + ((lane >> 3) & 1) * 8) * 2;
+  const uint32_t bl_base = bh_base + 128 * kTqStride * 2;
+  const int64_t n_rows = ra.n_groups * ra.rpg;
+  const int64_t rstep = (int64_t)gridDim.x * kTqWarps * 16;
+  // 16 rows into staging buffer `buf` with 16-byte cp.async copies (rows
+  // past the end are zero-filled)
+  auto stage = [&](int64_t r0, int buf) {
+    __half* dst = rows2 + buf * 16 * kTqStride;
+    // lanes 0..15 split one row address each; lane l copies 16-byte chunk l % 16
+    // of rows l / 16, l / 16 + 2, ...
+    int64_t my = -1;
+    if (lane < 16 && r0 + lane < n_rows) {
+      int64_t gg, tt;
+      ra.split(r0 + lane, gg, tt);
+      my = gg * vgs + tt * vrs;
+    }
+    const int cv = lane & 15;
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+      const int rr = (lane >> 4) + 2 * m;
+      const int64_t base = __shfl_sync(0xffffffffu, my, rr);
+      cp_async16(smem_u32(dst + rr * kTqStride + cv * 8), base >= 0 ? v + base + cv * 8 : v,
+                 base >= 0 ? 16u : 0u);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  int buf = 0;
+  int64_t r0 = ((int64_t)blockIdx.x * kTqWarps + warp) * 16;
+  if (r0 < n_rows) stage(r0, 0);
+  for (; r0 < n_rows; r0 += rstep, buf ^= 1) {
+    // prefetch the next 16 rows while this group is rotated and packed
+    if (r0 + rstep < n_rows) {
+      stage(r0 + rstep, buf ^ 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncwarp();
+    __half* rows = rows2 + buf * 16 * kTqStride;
+    const uint32_t a_base = smem_u32(rows) + a_off;
+    float nrm_lo = 0.f, nrm_hi = 0.f;  // norms of rows g and g + 8 (mode 0)
+    if (mode == 0) {
+      // lanes 2r, 2r + 1 sum halves of row r
+      const __half* rp = rows + (lane >> 1) * kTqStride + (lane & 1) * 64;
+      float ss = 0.f;
+      for (int j = 0; j < 64; ++j) {
+        const float x = __half2float(rp[j]);
+        ss = fmaf(x, x, ss);
+      }
+      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+      nrm_lo = sqrtf(__shfl_sync(0xffffffffu, ss, 2 * g));
+      nrm_hi = sqrtf(__shfl_sync(0xffffffffu, ss, 2 * (g + 8)));
+    }
+    float acc[16][4];
+#pragma unroll
+    for (int n = 0; n < 16; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+#pragma unroll 1
+    for (int kk = 0; kk < 8; ++kk) {  // rolled: keeps the kernel in the instruction cache
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4(a_base + kk * 32, a0, a1, a2, a3);
+#pragma unroll
+      for (int np = 0; np < 8; ++np) {
+        const uint32_t off = (np * 16 * kTqStride + kk * 16) * 2;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(bh_base + off, b0, b1, b2, b3);
+        mma_16816(acc[2 * np], a0, a1, a2, a3, b0, b1);
+        mma_16816(acc[2 * np + 1], a0, a1, a2, a3, b2, b3);
+        ldsm_x4(bl_base + off, b0, b1, b2, b3);
+        mma_16816(acc[2 * np], a0, a1, a2, a3, b0, b1);
+        mma_16816(acc[2 * np + 1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+    // codes; rows g (acc[.][0..1]) and g + 8 (acc[.][2..3])
+    uint8_t code[16][4];
+    float gsc[2][4];  // group scales of rows g, g + 8 (mode 1)
+    if (mode == 0) {
+      const float den0 = fmaxf(nrm_lo, 1e-8f), den1 = fmaxf(nrm_hi, 1e-8f);
+#pragma unroll
+      for (int n = 0; n < 16; ++n) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float x = __fdiv_rn(acc[n][e], e < 2 ? den0 : den1);
+          int q = 0;
+#pragma unroll
+          for (int j = 0; j < nbnd; ++j) q += (x > s_b[j]) ? 1 : 0;
+          code[n][e] = static_cast<uint8_t>(q);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {  // groups of 32 columns = 4 tiles
+        float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+        for (int n = 4 * q4; n < 4 * q4 + 4; ++n) {
+          s0 = fmaf(acc[n][0], acc[n][0], fmaf(acc[n][1], acc[n][1], s0));
+          s1 = fmaf(acc[n][2], acc[n][2], fmaf(acc[n][3], acc[n][3], s1));
+        }
+        s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
+        s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
+        s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+        s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+        const float sc0 = __half2float(__float2half_rn(sqrtf(s0 / 32.f)));
+        const float sc1 = __half2float(__float2half_rn(sqrtf(s1 / 32.f)));
+        gsc[0][q4] = sc0;
+        gsc[1][q4] = sc1;
+#pragma unroll
+        for (int n = 4 * q4; n < 4 * q4 + 4; ++n) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float sc = e < 2 ? sc0 : sc1;
+            int q = 0;
+#pragma unroll
+            for (int j = 0; j < nbnd; ++j) q += (acc[n][e] > __fmul_rn(s_b[j], sc)) ? 1 : 0;
+            code[n][e] = static_cast<uint8_t>(q);
+          }
+        }
+      }
+    }
+    // pack: OR the lanes' fields of each word across t, lane t writes words w % 4 == t
+#pragma unroll
+    for (int hrow = 0; hrow < 2; ++hrow) {
+      const int64_t r = r0 + g + 8 * hrow;
+      const bool ok = r < n_rows;
+      int64_t gg = 0, tt = 0;
+      if (ok) ra.split(r, gg, tt);
+      uint32_t* dst = packed + gg * pgs + tt * prs;
+      if (bits == 2) {
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+          uint32_t word = 0;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int n = 2 * w + h;
+            word |= (uint32_t)code[n][2 * hrow] << ((8 * h + 2 * t) * 2);
+            word |= (uint32_t)code[n][2 * hrow + 1] << ((8 * h + 2 * t + 1) * 2);
+          }
+          word |= __shfl_xor_sync(0xffffffffu, word, 1);
+          word |= __shfl_xor_sync(0xffffffffu, word, 2);
+          if (ok && (w & 3) == t) dst[w] = word;
+        }
+      } else {
+#pragma unroll
+        for (int w = 0; w < 16; ++w) {
+          uint32_t word = ((uint32_t)code[w][2 * hrow] << (2 * t * 4)) |
+                          ((uint32_t)code[w][2 * hrow + 1] << ((2 * t + 1) * 4));
+          word |= __shfl_xor_sync(0xffffffffu, word, 1);
+          word |= __shfl_xor_sync(0xffffffffu, word, 2);
+          if (ok && (w & 3) == t) dst[w] = word;
+        }
+      }
+      if (ok) {
+        if (mode == 0) {
+          if (t == 0) reinterpret_cast<float*>(scales)[gg * sgs + tt * srs] = hrow ? nrm_hi : nrm_lo;
+        } else {
+          reinterpret_cast<__half*>(scales)[gg * sgs + tt * srs + t] = __float2half_rn(gsc[hrow][t]);
+        }
+      }
+    }
+    __syncwarp();
+  }
+}
+
 // ------------------------------------------------------------- decode
 __global__ void __launch_bounds__(kWarpsPerCta * 32)
     value_decode_kernel(const uint32_t* packed, RowAddr ra, int64_t pgs, int64_t prs, int d,
@@ -315,6 +513,22 @@ int ss_value_encode_tq(const void* v, int v_dtype, int64_t n_groups, int64_t row
   count_dispatch("ss_value_encode_tq");
   const int64_t n = n_groups * rows_per_group;
   if (n <= 0) return SS_OK;
+  if (v_dtype == SS_F16 && d == 128 && (bits == 2 || bits == 4) &&
+      (mode == 0 || group_size == 32) &&
+      ((reinterpret_cast<uintptr_t>(v) | (uintptr_t)(v_group_stride * 2) |
+        (uintptr_t)(v_row_stride * 2)) & 15) == 0) {
+    const size_t smem_t = (size_t)(2 * 128 + kTqWarps * 2 * 16) * kTqStride * 2;
+    auto kern = bits == 2 ? encode_tq_mma_kernel<2> : encode_tq_mma_kernel<4>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_t);
+    int64_t blocks = (n + kTqWarps * 16 - 1) / (kTqWarps * 16);
+    const int64_t cap = sm_count();
+    if (blocks > cap) blocks = cap;
+    kern<<<static_cast<int>(blocks), kTqWarps * 32, smem_t, as_stream(stream)>>>(
+        reinterpret_cast<const __half*>(v), RowAddr{n_groups, rows_per_group}, v_group_stride,
+        v_row_stride, mode, rot, bnd, packed, p_group_stride, p_row_stride, scales,
+        s_group_stride, s_row_stride);
+    return check_launch("ss_value_encode_tq");
+  }
   const size_t smem = (size_t)d * d * 4;
   cudaFuncSetAttribute(encode_tq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   encode_tq_kernel<<<grid_rows(n), kWarpsPerCta * 32, smem, as_stream(stream)>>>(
