@@ -101,6 +101,63 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32)
   }
 }
 
+// Grouped min-max for fp16 rows of 128 values, 2- or 4-bit: a half-warp per row
+// (lane = one 16-byte chunk of 8 values), group min / max by shuffles among
+// the lanes of a group, the same fp32 arithmetic as the general kernel, and
+// codes packed straight into words (4-bit: one word per lane; 2-bit: lane
+// pairs). gs = group size (a multiple of 8 dividing 128).
+template <int BITS>
+__global__ void __launch_bounds__(256) encode_grouped_f16_kernel(
+    const __half* v, RowAddr ra, int64_t vgs, int64_t vrs, int gs, uint32_t* packed,
+    int64_t pgs, int64_t prs, float* scales, float* zeros, int64_t sgs, int64_t srs) {
+  constexpr int maxq = (1 << BITS) - 1;
+  const int lane = threadIdx.x & 31, half = lane >> 4, c = lane & 15;
+  const int lpg = gs >> 3;  // lanes per group
+  const int64_t n_rows = ra.n_groups * ra.rpg;
+  const int64_t step = (int64_t)gridDim.x * (blockDim.x >> 5) * 2;
+  for (int64_t r = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 2 + half;
+       r - half < n_rows; r += step) {
+    const bool ok = r < n_rows;
+    int64_t g = 0, t = 0;
+    if (ok) ra.split(r, g, t);
+    uint4 raw = make_uint4(0, 0, 0, 0);
+    if (ok) raw = *reinterpret_cast<const uint4*>(v + g * vgs + t * vrs + c * 8);
+    const __half* hv = reinterpret_cast<const __half*>(&raw);
+    float x[8];
+    float lo = INFINITY, hi = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      x[j] = __half2float(hv[j]);
+      lo = fminf(lo, x[j]);
+      hi = fmaxf(hi, x[j]);
+    }
+    for (int o = 1; o < lpg; o <<= 1) {
+      lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+      hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+    }
+    float sc = __fdiv_rn(__fsub_rn(hi, lo), static_cast<float>(maxq));
+    if (sc < 1e-8f) sc = 1e-8f;
+    uint32_t bitsw = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float qv = rintf(__fdiv_rn(__fsub_rn(x[j], lo), sc));
+      qv = fminf(fmaxf(qv, 0.f), static_cast<float>(maxq));
+      bitsw |= static_cast<uint32_t>(qv) << (j * BITS);
+    }
+    uint32_t* dst = packed + g * pgs + t * prs;
+    if (BITS == 4) {
+      if (ok) dst[c] = bitsw;
+    } else {  // 2-bit: 16 values per word = two lanes
+      const uint32_t other = __shfl_xor_sync(0xffffffffu, bitsw, 1);
+      if (ok && (c & 1) == 0) dst[c >> 1] = bitsw | (other << 16);
+    }
+    if (ok && (c % lpg) == 0) {
+      scales[g * sgs + t * srs + c / lpg] = sc;
+      zeros[g * sgs + t * srs + c / lpg] = lo;
+    }
+  }
+}
+
 // ------------------------------------------------------------- TurboQuant
 // rot is staged transposed in shared memory (s_rt[j][i] = R[i][j]) so that
 // lane i reads consecutive words when computing r_i = sum_j u_j R[i][j].
@@ -490,6 +547,20 @@ int ss_value_encode_grouped(const void* v, int v_dtype, int64_t n_groups, int64_
   count_dispatch("ss_value_encode_grouped");
   const int64_t n = n_groups * rows_per_group;
   if (n <= 0) return SS_OK;
+  if (v_dtype == SS_F16 && d == 128 && (bits == 2 || bits == 4) && group_size % 8 == 0 &&
+      group_size >= 8 &&
+      ((reinterpret_cast<uintptr_t>(v) | (uintptr_t)(v_group_stride * 2) |
+        (uintptr_t)(v_row_stride * 2)) & 15) == 0) {
+    int64_t blocks = (n + 15) / 16;  // 8 warps x 2 rows
+    const int64_t cap = 8LL * sm_count();
+    if (blocks > cap) blocks = cap;
+    auto kern = bits == 2 ? encode_grouped_f16_kernel<2> : encode_grouped_f16_kernel<4>;
+    kern<<<static_cast<int>(blocks), 256, 0, as_stream(stream)>>>(
+        reinterpret_cast<const __half*>(v), RowAddr{n_groups, rows_per_group}, v_group_stride,
+        v_row_stride, group_size, packed, p_group_stride, p_row_stride, scales, zeros,
+        s_group_stride, s_row_stride);
+    return check_launch("ss_value_encode_grouped");
+  }
   encode_grouped_kernel<<<grid_rows(n), kWarpsPerCta * 32, 0, as_stream(stream)>>>(
       v, v_dtype, RowAddr{n_groups, rows_per_group}, v_group_stride, v_row_stride, d, bits,
       group_size, packed, p_group_stride, p_row_stride, scales, zeros, s_group_stride,
