@@ -403,7 +403,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
   const int wgroup = warp / wps, slice = warp % wps;
   const int ctid = tid;                        // 0..255
   const int64_t q_off = p.tc + p.ttail - p.tq;
-  __half* Pw = reinterpret_cast<__half*>(smem + p.off_p) + warp * SL * 8;  // [64][8]
+  __half* Pw = reinterpret_cast<__half*>(smem + p.off_p) + warp * SL * 8;  // [32][8]
   uint8_t* vdq_w = smem + p.off_vdq + warp * (16 * D * 2);
   const uint32_t pw_addr = smem_u32(Pw) + (lane & 15) * 16;
   // ldmatrix.x4.trans addressing: lane -> (8x8 matrix mi, row mj)
@@ -419,6 +419,25 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
   // columns R..7 of every P slice stay zero
   for (int e = lane; e < SL * 8; e += 32)
     if ((e & 7) >= R) Pw[e] = __float2half_rn(0.f);
+
+  // Heavy (fp16 pass-through) blocks score on warp MMAs when their dims fit
+  // 16-dim k-steps: A = 16 tokens x 16 heavy dims straight from the stage,
+  // B = the unit's heavy query rows split into fp16 hi + lo (fp32-level
+  // accuracy); the 16x8 fp32 results go back to one token per lane through
+  // the warp's P slice, which is free between P.V and the next softmax.
+  const int hd = p.n_heavy * p.bd;
+  uint32_t heavy_off = p.off_aux;
+  if (p.vfmt != SS_V_F16) {
+    heavy_off += TILE * p.v_words * 4 + TILE * p.v_groups * (p.vs_dt == SS_F32 ? 4 : 2);
+    if (p.vz) heavy_off += TILE * p.v_groups * 4;
+  }
+  const bool heavy_mma_shape = (R == 4 || R == 8) && SL == 32 && p.n_heavy > 0 &&
+                               hd % 16 == 0 && hd <= 64 && (heavy_off & 15u) == 0;
+  uint32_t hq[4][2][2];  // [k-step][hi, lo][b0, b1]
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks)
+    hq[ks][0][0] = hq[ks][0][1] = hq[ks][1][0] = hq[ks][1][1] = 0u;
+  bool heavy_mma = false;
 
   int64_t tau = t_begin;
   uint32_t unit_no = 0;
@@ -451,6 +470,33 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
       named_bar_sync(1, (CW * 32));
       unit_codec_rows(p, ms.qo, ms.qc, ctid, (CW * 32));
       named_bar_sync(1, (CW * 32));
+      if (heavy_mma_shape) {
+        // B fragment of m16n8k16: b0 = B[2t, 2t+1][g], b1 = B[2t+8, 2t+9][g]
+        // with B[e][n] = codec-space query row n at heavy dim e.
+        const int g = lane >> 2, t = lane & 3;
+        bool finite = true;
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          if (ks * 16 >= hd) break;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float qv[2];
+            __half hi[2], lo[2];
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const int e = ks * 16 + h * 8 + 2 * t + j;
+              const int hb = e / p.bd;
+              qv[j] = g < R ? ms.qc[g][ms.heavy_pos[hb] * p.bd + (e - hb * p.bd)] : 0.f;
+              hi[j] = __float2half_rn(qv[j]);
+              lo[j] = __float2half_rn(qv[j] - __half2float(hi[j]));
+              finite = finite && isfinite(__half2float(hi[j])) && isfinite(__half2float(lo[j]));
+            }
+            hq[ks][0][h] = pack_halves2(hi[0], hi[1]);
+            hq[ks][1][h] = pack_halves2(lo[0], lo[1]);
+          }
+        }
+        heavy_mma = __all_sync(0xffffffffu, finite);
+      }
     }
     if (!ms.abort && !mbar_wait_bounded(&lut_bar, unit_no & 1, kWaitLimitNs)) {
       ms.abort = 1;
@@ -548,14 +594,48 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
             for (int r = 0; r < R; ++r) { s0[r] += e0[r]; s1[r] += e1[r]; }
           }
         }
-        if (p.n_heavy) {
-          int off = p.off_aux;
-          if (p.vfmt != SS_V_F16) {
-            off += TILE * p.v_words * 4 + TILE * p.v_groups * (p.vs_dt == SS_F32 ? 4 : 2);
-            if (p.vz) off += TILE * p.v_groups * 4;
+        if (heavy_mma) {
+          // lane -> ldmatrix row: token (lane & 15) of the 16-token tile,
+          // heavy dims +8 for lanes 16..31 (matrices a0..a3 of m16n8k16)
+          const uint32_t ha = smem_u32(st + heavy_off) +
+                              (uint32_t)((slice * SL + (lane & 15)) * hd * 2 + (lane >> 4) * 16);
+          const int g = lane >> 2, t = lane & 3;
+          float* scr = reinterpret_cast<float*>(Pw);  // [32 tokens][4 rows] fp32
+          float c[2][4];
+#pragma unroll
+          for (int mt = 0; mt < 2; ++mt) {
+            c[mt][0] = c[mt][1] = c[mt][2] = c[mt][3] = 0.f;
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+              if (ks * 16 >= hd) break;
+              uint32_t a0, a1, a2, a3;
+              ldsm_x4(ha + (uint32_t)(mt * 16 * hd * 2 + ks * 32), a0, a1, a2, a3);
+              mma_16816(c[mt], a0, a1, a2, a3, hq[ks][1][0], hq[ks][1][1]);
+              mma_16816(c[mt], a0, a1, a2, a3, hq[ks][0][0], hq[ks][0][1]);
+            }
           }
-          const uint16_t* h0 = reinterpret_cast<const uint16_t*>(st + off) + (size_t)tok0 * p.n_heavy * p.bd;
-          const uint16_t* h1 = reinterpret_cast<const uint16_t*>(st + off) + (size_t)tok1 * p.n_heavy * p.bd;
+#pragma unroll
+          for (int half = 0; half < R / 4; ++half) {
+            __syncwarp();  // previous readers of the P slice are done
+            if ((t >> 1) == half) {
+              const int cc = (2 * t) & 3;
+#pragma unroll
+              for (int mt = 0; mt < 2; ++mt) {
+                *reinterpret_cast<float2*>(scr + (mt * 16 + g) * 4 + cc) = make_float2(c[mt][0], c[mt][1]);
+                *reinterpret_cast<float2*>(scr + (mt * 16 + g + 8) * 4 + cc) = make_float2(c[mt][2], c[mt][3]);
+              }
+            }
+            __syncwarp();
+            const float4 hv = *reinterpret_cast<const float4*>(scr + lane * 4);
+            s0[half * 4 + 0] += hv.x;
+            s0[half * 4 + 1] += hv.y;
+            s0[half * 4 + 2] += hv.z;
+            s0[half * 4 + 3] += hv.w;
+          }
+          __syncwarp();  // scratch reads done before the P store
+        } else if (p.n_heavy) {
+          const uint16_t* h0 = reinterpret_cast<const uint16_t*>(st + heavy_off) + (size_t)tok0 * p.n_heavy * p.bd;
+          const uint16_t* h1 = reinterpret_cast<const uint16_t*>(st + heavy_off) + (size_t)tok1 * p.n_heavy * p.bd;
           for (int hj = 0; hj < p.n_heavy; ++hj) {
             const int b = ms.heavy_pos[hj];
             for (int j = 0; j < p.bd; ++j) {
@@ -640,7 +720,12 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
         m_w[r] = mn;
       }
       // this lane's weights for all rows in one store per token
-      if constexpr (R == 4 || R == 8) {
+      if constexpr (R == 4 && TPL == 1) {
+        // full 16-byte row: columns 4..7 rewritten as zero (the heavy-block
+        // scratch may have used them)
+        *reinterpret_cast<uint4*>(Pw + lane * 8) =
+            make_uint4(pack_halves2(ph0[0], ph0[1]), pack_halves2(ph0[2], ph0[3]), 0u, 0u);
+      } else if constexpr (R == 4 || R == 8) {
 #pragma unroll
         for (int r4 = 0; r4 < R; r4 += 4) {
           *reinterpret_cast<uint2*>(Pw + lane * 8 + r4) =

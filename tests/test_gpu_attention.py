@@ -232,6 +232,38 @@ def test_mixed_precision_heavy_blocks_exact_scoring(ss, hq):
     assert G.rel_err(out, want) < REL
 
 
+@pytest.mark.parametrize("n_heavy,hq,qdt,vals", [
+    (2, 8, torch.float16, "fp16"), (4, 16, torch.float32, "fp16"), (8, 8, torch.float32, "fp16"),
+    (8, 16, torch.float16, "grouped2"), (3, 8, torch.float32, "fp16"), (6, 16, torch.float16, "fp16"),
+    (12, 8, torch.float16, "grouped2"), (4, 8, torch.bfloat16, "grouped2")])
+def test_heavy_block_scoring_shapes(ss, n_heavy, hq, qdt, vals):
+    """Heavy-block dot products over every heavy width: 16/32/64 heavy dims
+    take the warp-MMA path (fp16 keys x hi+lo split queries), 24/48/96 the
+    per-lane path; fp32 and bf16 queries exercise the lo half of the split."""
+    rng = np.random.default_rng(40 + n_heavy)
+    qc = I.heavy_tailed_queries(2048, 128, seed=8)
+    kc = rng.standard_normal((2048, 128)).astype(np.float32)
+    codec = ss.SunShapeBlockCodec(head_dim=128, mode="profileperm_mixed_precision", n_heavy=n_heavy)
+    codec.fit(qc, kc, kmeans_iters=3, seed=0)
+    assert codec.n_heavy_blocks == n_heavy
+    kw = {} if vals == "fp16" else dict(value_backend="grouped", value_bits=2, buffer_size=0)
+    cache = ss.create_kv_cache(codec, n_kv_heads=2, **kw)
+    kk, vv = I.kv_stream(11, 1, 2, 1000, 128)
+    vv = vv * 2.0
+    cache.update_and_fetch(kk, vv)
+    q = torch.tensor(I.decode_queries(12, 1, hq, 1, 128), device="cuda").to(qdt) * 3
+    out = ss.sunshape_sdpa(q, cache, 1 / math.sqrt(128))
+    khat = torch.stack([torch.stack([codec(torch.tensor(kk[0, h], device="cuda")) for h in range(2)])])
+    vt = torch.tensor(vv, device="cuda")
+    if vals != "fp16":
+        vc = ss.GroupedValueCodec(head_dim=128, bits=2, group_size=64)
+        p_, s_, z_ = vc.quantize(vt.half())
+        vt = vc.dequantize(p_, s_, z_)
+    want = G.attention(G.scaled_queries(q, 1 / math.sqrt(128)), khat, vt.float())
+    tol = 4e-3 if qdt == torch.bfloat16 else 2e-3  # bf16 output: half an ulp is 2^-9 relative
+    assert G.rel_err(out, want) < tol, G.rel_err(out, want)
+
+
 def test_empty_cache_returns_zeros(ss, cfg1_codec):
     cache = ss.create_kv_cache(cfg1_codec, n_kv_heads=2)
     q = torch.randn((1, 4, 1, 128), device="cuda").half()
