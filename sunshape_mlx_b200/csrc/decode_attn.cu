@@ -138,7 +138,6 @@ __device__ __forceinline__ uint32_t vtile_addr(uint32_t base, int tile, int tok,
 struct Misc {  // small shared-memory state
   float qo[8][128];     // scaled queries, original basis
   float qc[8][128];     // scaled queries, codec space
-  float o[8][128];      // finalisation staging
   float mrow[8], lrow[8];
   float levels[16];
   float2 lvpair[16];    // 2-bit values: levels of the two codes of each 4-bit nibble
@@ -263,7 +262,7 @@ __global__ void __launch_bounds__(kLutThreads) lut_kernel(const __grid_constant_
   }
 }
 
-template <int R, int D, int NBC, int CW>
+template <int R, int D, int NBC, int CW, bool HV>
 __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
     const __grid_constant__ DecodeParams p, const __grid_constant__ CUtensorMap map_v,
     const __grid_constant__ CUtensorMap map_vt) {
@@ -431,12 +430,11 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
     heavy_off += TILE * p.v_words * 4 + TILE * p.v_groups * (p.vs_dt == SS_F32 ? 4 : 2);
     if (p.vz) heavy_off += TILE * p.v_groups * 4;
   }
-  const bool heavy_mma_shape = (R == 4 || R == 8) && SL == 32 && p.n_heavy > 0 &&
+  const bool heavy_mma_shape = HV && (R == 4 || R == 8) && SL == 32 && p.n_heavy > 0 &&
                                hd % 16 == 0 && hd <= 64 && (heavy_off & 15u) == 0;
-  uint32_t hq[4][2][2];  // [k-step][hi, lo][b0, b1]
-#pragma unroll
-  for (int ks = 0; ks < 4; ++ks)
-    hq[ks][0][0] = hq[ks][0][1] = hq[ks][1][0] = hq[ks][1][1] = 0u;
+  // B fragments [k-step][hi, lo][lane] (b0, b1), kept in the codec-query rows
+  // once those are built into fragments (nothing else reads them then)
+  const uint2* hqs = reinterpret_cast<const uint2*>(&ms.qc[0][0]);
   bool heavy_mma = false;
 
   int64_t tau = t_begin;
@@ -475,6 +473,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
         // with B[e][n] = codec-space query row n at heavy dim e.
         const int g = lane >> 2, t = lane & 3;
         bool finite = true;
+        uint32_t hq[4][2][2];  // [k-step][hi, lo][b0, b1]
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) {
           if (ks * 16 >= hd) break;
@@ -496,6 +495,17 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
           }
         }
         heavy_mma = __all_sync(0xffffffffu, finite);
+        named_bar_sync(1, (CW * 32));  // every warp has read the codec rows
+        if (heavy_mma && warp == 0) {
+          uint2* dst = reinterpret_cast<uint2*>(&ms.qc[0][0]);
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            if (ks * 16 >= hd) break;
+            dst[(ks * 2 + 0) * 32 + lane] = make_uint2(hq[ks][0][0], hq[ks][0][1]);
+            dst[(ks * 2 + 1) * 32 + lane] = make_uint2(hq[ks][1][0], hq[ks][1][1]);
+          }
+        }
+        named_bar_sync(1, (CW * 32));
       }
     }
     if (!ms.abort && !mbar_wait_bounded(&lut_bar, unit_no & 1, kWaitLimitNs)) {
@@ -601,17 +611,17 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
                               (uint32_t)((slice * SL + (lane & 15)) * hd * 2 + (lane >> 4) * 16);
           const int g = lane >> 2, t = lane & 3;
           float* scr = reinterpret_cast<float*>(Pw);  // [32 tokens][4 rows] fp32
-          float c[2][4];
+          float c[2][4] = {};
 #pragma unroll
-          for (int mt = 0; mt < 2; ++mt) {
-            c[mt][0] = c[mt][1] = c[mt][2] = c[mt][3] = 0.f;
+          for (int ks = 0; ks < 4; ++ks) {
+            if (ks * 16 >= hd) break;
+            const uint2 bh = hqs[(ks * 2 + 0) * 32 + lane], bl = hqs[(ks * 2 + 1) * 32 + lane];
 #pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
-              if (ks * 16 >= hd) break;
+            for (int mt = 0; mt < 2; ++mt) {
               uint32_t a0, a1, a2, a3;
               ldsm_x4(ha + (uint32_t)(mt * 16 * hd * 2 + ks * 32), a0, a1, a2, a3);
-              mma_16816(c[mt], a0, a1, a2, a3, hq[ks][1][0], hq[ks][1][1]);
-              mma_16816(c[mt], a0, a1, a2, a3, hq[ks][0][0], hq[ks][0][1]);
+              mma_16816(c[mt], a0, a1, a2, a3, bl.x, bl.y);
+              mma_16816(c[mt], a0, a1, a2, a3, bh.x, bh.y);
             }
           }
 #pragma unroll
@@ -720,7 +730,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
         m_w[r] = mn;
       }
       // this lane's weights for all rows in one store per token
-      if constexpr (R == 4 && TPL == 1) {
+      if constexpr (HV && R == 4 && TPL == 1) {
         // full 16-byte row: columns 4..7 rewritten as zero (the heavy-block
         // scratch may have used them)
         *reinterpret_cast<uint4*>(Pw + lane * 8) =
@@ -884,6 +894,8 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
     float* wo = lut;                                  // [8][R][D]
     float* wm = lut + CW * R * D;         // [8][R]
     float* wl = wm + CW * R;              // [8][R]
+    // merged unit rows for finalisation, after the per-warp scratch
+    float (*mo)[D] = reinterpret_cast<float (*)[D]>(lut + CW * R * (D + 2));
     {
       const int n0 = 2 * (lane & 3);
       const int m0 = lane >> 2;
@@ -916,7 +928,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
         O = fmaf(wo[(w * R + r) * D + j], wt, O);
         L = fmaf(wl[w * R + r], wt, L);
       }
-      ms.o[r][j] = O;
+      mo[r][j] = O;
       if (j == 0) { ms.mrow[r] = mstar; ms.lrow[r] = L; }
     }
     named_bar_sync(1, (CW * 32));
@@ -931,7 +943,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
       float* slot = p.slots + ((size_t)u * p.max_cov + (cta - first)) * R * row_floats;
       for (int e = ctid; e < R * row_floats; e += (CW * 32)) {
         const int r = e / row_floats, j = e - r * row_floats;
-        slot[e] = j < D ? ms.o[r][j] : (j == D ? ms.mrow[r] : ms.lrow[r]);
+        slot[e] = j < D ? mo[r][j] : (j == D ? ms.mrow[r] : ms.lrow[r]);
       }
       __threadfence();
       named_bar_sync(1, (CW * 32));
@@ -960,7 +972,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
             O = fmaf(__ldcg(row + j), w, O);
             L = fmaf(__ldcg(row + D + 1), w, L);
           }
-          ms.o[r][j] = O;
+          mo[r][j] = O;
           if (j == 0) { ms.mrow[r] = mstar; ms.lrow[r] = L; }
         }
         named_bar_sync(1, (CW * 32));
@@ -975,17 +987,17 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
         const int qh = hh * p.nrep + rep;
         if (p.part_out) {
           float* row = p.part_out + (((int64_t)bb * p.hq + qh) * p.tq + tqi) * (D + 2);
-          row[j] = ms.o[r][j];
+          row[j] = mo[r][j];
           if (j == 0) { row[D] = ms.mrow[r]; row[D + 1] = ms.lrow[r]; }
         } else {
           const float inv = ms.lrow[r] > 0.f ? 1.f / ms.lrow[r] : 0.f;
           float v;
           if (p.v_rot) {
             float a = 0.f;
-            for (int i = 0; i < D; ++i) a = fmaf(ms.o[r][i], __ldg(p.v_rot + i * D + j), a);
+            for (int i = 0; i < D; ++i) a = fmaf(mo[r][i], __ldg(p.v_rot + i * D + j), a);
             v = a * inv;
           } else {
-            v = ms.o[r][j] * inv;
+            v = mo[r][j] * inv;
           }
           store_from_f32(p.out, p.odt, bb * p.o_sb + qh * p.o_sh + tqi * p.o_st + j, v);
         }
@@ -1101,9 +1113,10 @@ int make_plan_r(const ss_decode_args* a, Plan& pl, int r_cap, int cw) {
   const size_t vdq = (a->vfmt == SS_V_QUANT) ? (size_t)cw * 16 * a->d * 2 : 0;
   // the LUT region doubles as the per-warp merge scratch at unit ends
   size_t lut = (size_t)nb * a->k * R * 4;
-  const size_t scratch = (size_t)cw * R * (a->d + 2) * 4;
+  // per-warp merge scratch + the merged rows of the unit
+  const size_t scratch = (size_t)cw * R * (a->d + 2) * 4 + (size_t)R * a->d * 4;
   if (lut < scratch) lut = scratch;
-  const size_t pbytes = (size_t)cw * 64 * 16;
+  const size_t pbytes = (size_t)cw * slice_tokens(R) * 16;  // per-warp P slice [tokens][8] fp16
   fixed = vdq + ((lut + 127) & ~size_t(127)) + pbytes + ((sizeof(Misc) + 127) & ~size_t(127)) + 1024;
   if (fixed + 2 * (size_t)pl.stage_bytes > kSmemBudget)
     return fail(SS_ERR_UNSUPPORTED, "ss_decode_attn: configuration exceeds shared memory");
@@ -1175,8 +1188,16 @@ int launch_decode(const DecodeParams& p, const CUtensorMap& mv, const CUtensorMa
   int rc = check_launch("ss_decode_attn (tables)");
   if (rc != SS_OK) return rc;
   const bool nb16 = p.nb == 16 && p.k == 256;
-  auto kern = cw == 12 ? (nb16 ? decode_attn_kernel<R, D, 16, 12> : decode_attn_kernel<R, D, 0, 12>)
-                       : (nb16 ? decode_attn_kernel<R, D, 16, 8> : decode_attn_kernel<R, D, 0, 8>);
+  // the warp-MMA heavy-block variant only where it can apply (it holds the
+  // query fragments in registers for the whole unit)
+  const int hd = p.n_heavy * p.bd;
+  const bool hv = (R == 4 || R == 8) && D == 128 && p.n_heavy > 0 && hd % 16 == 0 && hd <= 64;
+  constexpr bool kHv = (R == 4 || R == 8) && D == 128;
+  auto kern = cw == 12 ? (nb16 ? decode_attn_kernel<R, D, 16, 12, false> : decode_attn_kernel<R, D, 0, 12, false>)
+                       : (nb16 ? decode_attn_kernel<R, D, 16, 8, false> : decode_attn_kernel<R, D, 0, 8, false>);
+  if (kHv && hv)
+    kern = cw == 12 ? (nb16 ? decode_attn_kernel<R, D, 16, 12, kHv> : decode_attn_kernel<R, D, 0, 12, kHv>)
+                    : (nb16 ? decode_attn_kernel<R, D, 16, 8, kHv> : decode_attn_kernel<R, D, 0, 8, kHv>);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess)
