@@ -366,6 +366,42 @@ def _build_cfg5(device, rank, world):
     q = torch.randn((1, c["HQ"], 1, D), generator=g, device=device).half()
     return codec, cache, q
 
+CFG4 = dict(B=32, HQ=32, HKV=8, T=4096, LAYERS=32, bytes_per_th=32 + 32,
+            workload="cfg4 attention: 32 layers of decode attention, B=32/GPU, 32q/8kv heads, "
+                     "head_dim 128, T_kv 4096, block-VQ keys AND values (block_dim 4, 256 centroids, "
+                     "32 blocks; value_backend 'sunshape'), buffer_size 0, 1 query token/step/layer")
+
+
+def _build_cfg4(device):
+    """32 layers of (B, 8, 4096) caches with block-VQ keys and values. One key
+    codec and one value codec (fit once) serve every layer; each layer holds
+    its own seeded tokens."""
+    import torch
+    import sunshape_mlx_b200 as ss
+
+    c = CFG4
+    qc, kc, sig = _calibration()
+    kcodec = ss.SunShapeBlockCodec(head_dim=D, block_dim=4, n_centroids=KC, device=device)
+    kcodec.fit(qc, kc, kmeans_iters=25, seed=0)
+    rng = np.random.default_rng(44)
+    vcal = rng.standard_normal((4096, D)).astype(np.float16)
+    vcodec = ss.SunShapeBlockCodec(head_dim=D, block_dim=4, n_centroids=KC, device=device)
+    vcodec.fit(qc, vcal, kmeans_iters=25, seed=1)
+    sig_t = torch.tensor(sig, device=device)
+    caches = []
+    for layer in range(c["LAYERS"]):
+        cache = ss.create_kv_cache(kcodec, n_kv_heads=c["HKV"], value_backend="sunshape",
+                                   value_bits=8, value_codec=vcodec, buffer_size=0)
+        g = torch.Generator(device=device).manual_seed(4000 + layer)
+        k = (torch.randn((c["B"], c["HKV"], c["T"], D), generator=g, device=device) * sig_t).half()
+        v = torch.randn((c["B"], c["HKV"], c["T"], D), generator=g, device=device).half()
+        cache.append(k, v)
+        caches.append(cache)
+    del k, v
+    g = torch.Generator(device=device).manual_seed(4999)
+    q = torch.randn((c["B"], c["HQ"], 1, D), generator=g, device=device).half()
+    return kcodec, caches, q
+
 
 def run_config(args, world, rank, local):
     import torch
@@ -373,15 +409,26 @@ def run_config(args, world, rank, local):
     from sunshape_mlx_b200.attention import PreparedDecode
     from sunshape_mlx_b200 import splitkv
 
-    c = CFG3 if args.config == 3 else CFG5
+    c = {3: CFG3, 4: CFG4, 5: CFG5}[args.config]
+    layers = c.get("LAYERS", 1)
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     scale = 1 / math.sqrt(D)
     if args.config == 3:
         codec, cache, q = _build_cfg3(device)
+    elif args.config == 4:
+        codec, caches, q = _build_cfg4(device)
+        cache = caches[0]
     else:
         codec, cache, q = _build_cfg5(device, rank, world)
-    if world > 1 and args.config == 5:
+    if args.config == 4:
+        preps = [PreparedDecode(q, cl, scale) for cl in caches]
+
+        def step():
+            for pr in preps:
+                pr.run()
+        launches = 2 * layers
+    elif world > 1 and args.config == 5:
         def step():
             splitkv.splitkv_sdpa(q, cache, scale)
         launches = 3  # table + decode (partials) + merge; plus the NCCL all-gather
@@ -389,6 +436,12 @@ def run_config(args, world, rank, local):
         prep = PreparedDecode(q, cache, scale)
         step = prep.run
         launches = 2
+    if args.profile:
+        for _ in range(args.warmup + args.steps):
+            step()
+        torch.cuda.synchronize()
+        print("profile run done", flush=True)
+        return None
 
     def barrier():
         if world > 1:
@@ -422,18 +475,21 @@ def run_config(args, world, rank, local):
         return None
     peak, peak_kind = _peaks()
     per_rank_tokens = c["T"] // world if args.config == 5 else c["T"]
-    alg_bytes = c["B"] * c["HKV"] * per_rank_tokens * c["bytes_per_th"] + 2 * c["B"] * c["HQ"] * D * 2
+    alg_bytes = layers * (c["B"] * c["HKV"] * per_rank_tokens * c["bytes_per_th"]
+                          + 2 * c["B"] * c["HQ"] * D * 2)
     achieved = alg_bytes / (ms / 1e3) / 1e9
-    nq = c["B"] * c["HQ"] * (world if args.config == 3 else 1)
+    weak = args.config in (3, 4)
+    nq = c["B"] * c["HQ"] * layers * (world if weak else 1)
     line = {
         "metric": METRIC, "value": nq / (ms / 1e3), "unit": "queries/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak" if args.config == 3 else "strong", "vs_baseline": None, "dtype": "f16",
+        "scaling": "weak" if weak else "strong", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (seeded anisotropic keys, N(0,1) fp16 values/queries)",
-        "config": {"workload": c["workload"], "global_batch": c["B"] * (world if args.config == 3 else 1),
-                   "seq_len": c["T"], "parallelism": (f"dp{world} (batch shards)" if args.config == 3
+        "config": {"workload": c["workload"], "global_batch": c["B"] * (world if weak else 1),
+                   "seq_len": c["T"], "parallelism": (f"dp{world} (batch shards)" if weak
                                                       else f"split-KV x{world} (token shards, NCCL all-gather + LSE merge)"),
-                   "l2": f"inputs larger than L2 ({alg_bytes / 1e6:.0f} MB streamed per step per GPU)"},
+                   "l2": f"inputs larger than L2 ({alg_bytes / 1e6:.0f} MB streamed per step per GPU)",
+                   "queries_per_step": nq},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_source": peak_kind,
                      "frac_of_8TBs_nominal": achieved / 8000.0, "traffic": None,
@@ -456,7 +512,8 @@ def _cpu_baseline_cfg(cfg, codec, cache, q, budget_s: float = 8.0):
     state = {"mode": "profileperm_baseline", "head_dim": D, "block_dim": BD, "n_blocks": NB,
              "n_centroids": KC, "centroids": st["centroids"].numpy(),
              "permutation": st["permutation"].numpy(), "heavy": np.zeros(NB, bool)}
-    c = CFG3 if cfg == 3 else CFG5
+    c = {3: CFG3, 4: CFG4, 5: CFG5}[cfg]
+    state.update(block_dim=codec.block_dim, n_blocks=codec.n_blocks)
     rep = c["HQ"] // c["HKV"]
     idx = cache.key_indices[:1, :1].cpu().numpy()
     vals = cache.values[:1, :1].float().cpu().numpy()  # dequantised as the reference does
@@ -690,8 +747,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", type=int, choices=[2, 3, 5], default=2,
-                    help="decode configuration (BASELINE configs 2, 3, 5)")
+    ap.add_argument("--config", type=int, choices=[2, 3, 4, 5], default=2,
+                    help="decode configuration (BASELINE configs 2, 3, 5; 4 = config-4 attention)")
     ap.add_argument("--assign", action="store_true",
                     help="benchmark the cache-fill quantize (ss_vq_assign) instead of decode")
     ap.add_argument("--assign-path", choices=["tensor", "simt", "auto"], default="tensor")

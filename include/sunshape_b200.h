@@ -207,7 +207,7 @@ int ss_value_decode(const uint32_t* packed, int64_t n_groups, int64_t rows_per_g
  * stride (elements) and must hold at least round_up(tc, 128) rows per pair
  * (cache capacity); the kernel streams whole 128-token tiles.
  * -------------------------------------------------------------------------- */
-enum ss_vfmt { SS_V_F16 = 0, SS_V_QUANT = 1 };
+enum ss_vfmt { SS_V_F16 = 0, SS_V_QUANT = 1, SS_V_VQ = 2 };
 
 typedef struct ss_decode_args {
   /* queries (b, hq, tq, d), element strides */
@@ -235,6 +235,13 @@ typedef struct ss_decode_args {
   const float* v_zeros; int64_t vz_pair_stride;        /* rows d/v_group or NULL */
   float v_levels[16];        /* level table for SS_V_QUANT */
   const float* v_rot;        /* f32 (d,d): value = r @ R, or NULL */
+  /* SunShape block-VQ values (SS_V_VQ, value_backend "sunshape", cache.py:785-812):
+   * u8 rows of d/v_bd centroid indices; value (codec space) = concat of
+   * v_cents[b][idx[b]]; the codec's inverse transform goes in v_rot. d = 128,
+   * v_bd in {4, 8, 16}, v_k <= 256. */
+  const uint8_t* v_idx; int64_t vi_pair_stride;
+  const uint16_t* v_cents;   /* f16 [d/v_bd][v_k][v_bd] */
+  int v_bd, v_k;
   /* fp16 tail (hybrid buffer): keys in the original basis; values in the
    * original basis, or already rotated (v R^T) when v_rot is set */
   int64_t ttail;

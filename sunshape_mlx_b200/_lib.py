@@ -21,7 +21,7 @@ SS_OK = 0
 STATUS_NAMES = {1: "bad argument", 2: "unsupported", 3: "CUDA error", 4: "timeout",
                 5: "workspace"}
 SS_F32, SS_F16, SS_BF16 = 0, 1, 2
-SS_V_F16, SS_V_QUANT = 0, 1
+SS_V_F16, SS_V_QUANT, SS_V_VQ = 0, 1, 2
 
 _DTYPE_CODE = {torch.float32: SS_F32, torch.float16: SS_F16, torch.bfloat16: SS_BF16}
 
@@ -61,6 +61,7 @@ class DecodeArgs(C.Structure):
         ("v_zeros", vp), ("vz_pair_stride", i64),
         ("v_levels", f32 * 16),
         ("v_rot", vp),
+        ("v_idx", vp), ("vi_pair_stride", i64), ("v_cents", vp), ("v_bd", i32), ("v_k", i32),
         ("ttail", i64),
         ("k_tail", vp), ("v_tail", vp), ("tail_pair_stride", i64),
         ("causal", i32),

@@ -74,10 +74,18 @@ def _fill_args(q: torch.Tensor, centroids: torch.Tensor, perm, scale: float, spe
         if n_heavy:
             a.kheavy = kh.data_ptr()
             a.kheavy_pair_stride = kh.stride(1)
+        vi = spec.get("vi")
         if v is not None:
             a.vfmt = L.SS_V_F16
             a.v = v.data_ptr()
             a.v_pair_stride = v.stride(1)
+        elif vi is not None:
+            a.vfmt = L.SS_V_VQ
+            a.v_idx = vi.data_ptr()
+            a.vi_pair_stride = vi.stride(1)
+            vc = spec["v_cents"]
+            a.v_cents = vc.data_ptr()
+            a.v_k, a.v_bd = vc.shape[1], vc.shape[2]
         else:
             a.vfmt = L.SS_V_QUANT
             a.vq = vq.data_ptr()
@@ -95,7 +103,7 @@ def _fill_args(q: torch.Tensor, centroids: torch.Tensor, perm, scale: float, spe
             lv = list(spec["levels"]) + [0.0] * (16 - len(spec["levels"]))
             a.v_levels = (C.c_float * 16)(*lv)
     else:
-        a.vfmt = L.SS_V_F16 if v is not None or vq is None else L.SS_V_QUANT
+        a.vfmt = L.SS_V_F16 if v is not None or vq is None else L.SS_V_QUANT  # tail only
     vr = spec.get("v_rot")
     if vr is not None:
         vr = vr.contiguous()

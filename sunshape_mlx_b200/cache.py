@@ -324,6 +324,7 @@ class HybridSunShapeKVCache:
         # TurboQuant values are attended in the rotated basis; the fp16 tail is
         # kept there too (v R^T) so one accumulator covers all tokens.
         self._value_buffer_rot = None
+        self._vq_tables = None   # (key, fp16 value centroids, inverse-transform matrix)
         self._key_indices = None
         self._key_heavy = None
         self._values_packed = None
@@ -422,16 +423,20 @@ class HybridSunShapeKVCache:
                                      torch.float16, self.device)
             self._value_buffer = _grow(self._value_buffer, (B, H, size, D), self._buffer_offset,
                                        torch.float16, self.device)
-            if self.value_backend == "turboquant":
+            if self.value_backend == "turboquant" or self._vq_transformed():
                 self._value_buffer_rot = _grow(self._value_buffer_rot, (B, H, size, D),
                                                self._buffer_offset, torch.float16, self.device)
         b0 = self._buffer_offset
         self._key_buffer[:, :, b0:b0 + T] = k
         self._value_buffer[:, :, b0:b0 + T] = v
         if self._value_buffer_rot is not None:
-            from .rotation import _matmul_f32
-            rt = self._value_codec_impl.rotation_t
-            self._value_buffer_rot[:, :, b0:b0 + T] = _matmul_f32(v.float(), rt).half()
+            if self.value_backend == "turboquant":
+                from .rotation import _matmul_f32
+                rt = self._value_codec_impl.rotation_t
+                self._value_buffer_rot[:, :, b0:b0 + T] = _matmul_f32(v.float(), rt).half()
+            else:  # block-VQ values: the value codec's own basis
+                self._value_buffer_rot[:, :, b0:b0 + T] = \
+                    self.value_codec._forward_transform(v.float()).half()
         self._buffer_offset += T
         if self._buffer_offset > self.buffer_size:
             self._flush_buffer(B, self._buffer_offset - self.buffer_size)
@@ -535,6 +540,27 @@ class HybridSunShapeKVCache:
     def can_fuse_value_dequant(self) -> bool:
         return self.value_backend == "grouped" and self._compressed_offset > 0
 
+    def _vq_transformed(self) -> bool:
+        vc = self.value_codec
+        return self.value_backend == "sunshape" and (vc._is_perm() or vc.use_rotation)
+
+    def _vq_value_tables(self):
+        """Block-VQ values for the fused decode: the value centroids in fp16
+        (the dtype the reference's cache returns dequantised values in,
+        cache.py:785-812) and the codec's inverse transform as a (D, D) matrix
+        M with x = y @ M (a permutation matrix, the rotation, or None)."""
+        vc = self.value_codec
+        key = (vc.centroids.data_ptr(), vc.centroids._version, vc.use_rotation,
+               vc.permutation.data_ptr(), vc.permutation._version)
+        if self._vq_tables is None or self._vq_tables[0] != key:
+            cents = vc.centroids.to(torch.float16).contiguous()
+            vrot = None
+            if vc._is_perm() or vc.use_rotation:
+                eye = torch.eye(self.head_dim, dtype=torch.float32, device=self.device)
+                vrot = vc._inverse_transform(eye).contiguous()
+            self._vq_tables = (key, cents, vrot)
+        return self._vq_tables[1], self._vq_tables[2]
+
     # ------------------------------------------------------------ fused-attention view
     def attention_spec(self) -> dict:
         spec = dict(tc=self._compressed_offset, cap=self._compressed_capacity)
@@ -546,11 +572,10 @@ class HybridSunShapeKVCache:
             if self.value_backend == "fp16":
                 spec["v"] = self._values_fp16
             elif self.value_backend == "sunshape":
-                cap = self._compressed_capacity
-                full = torch.zeros((self._batch, self.n_kv_heads, cap, self.head_dim),
-                                   dtype=torch.float16, device=self.device)
-                full[:, :, :self._compressed_offset] = self._compressed_values(torch.float16)
-                spec["v"] = full
+                cents, vrot = self._vq_value_tables()
+                spec.update(vi=self._value_indices, v_cents=cents)
+                if vrot is not None:
+                    spec["v_rot"] = vrot
             elif self.value_backend == "grouped":
                 spec.update(vq=self._values_packed, vs=self._value_scales, vz=self._value_zeros,
                             bits=vc.bits, group=vc.group_size, levels=vc.levels(self.device))
@@ -564,7 +589,8 @@ class HybridSunShapeKVCache:
             vt = self._value_buffer_rot if self._value_buffer_rot is not None else self._value_buffer
             spec.update(k_tail=self._key_buffer, v_tail=vt, ttail=self._buffer_offset)
             if self._value_buffer_rot is not None and "v_rot" not in spec:
-                spec["v_rot"] = self._value_codec_impl.rotation
+                spec["v_rot"] = (self._value_codec_impl.rotation if self.value_backend == "turboquant"
+                                 else self._vq_value_tables()[1])
         return spec
 
     # ------------------------------------------------------------ accounting

@@ -74,6 +74,11 @@ struct DecodeParams {
   int64_t vz_ps;
   float levels[16];
   const float* v_rot;
+  const uint8_t* vidx;       // SS_V_VQ: u8 rows v_nb
+  int64_t vi_ps;
+  const uint16_t* vcents;    // SS_V_VQ: f16 [v_nb][v_k][v_bd]
+  int v_bd, v_k, v_nb;
+  uint32_t v_tile_bytes;     // stage bytes of one tile's value stream (quantized / VQ)
   // tail
   const uint16_t* k_tail;
   const uint16_t* v_tail;
@@ -95,7 +100,7 @@ struct DecodeParams {
   float* lut_g;             // per-unit query x centroid tables [unit][nb][k][R]
   uint32_t lut_unit_bytes;
   // shared-memory carve-up (bytes from the 1024-aligned base)
-  uint32_t off_stage, stage_bytes, off_idx, off_aux, off_vdq, off_lut, off_p, off_misc;
+  uint32_t off_stage, stage_bytes, off_idx, off_aux, off_vdq, off_lut, off_p, off_misc, off_vtab;
 };
 
 // Tokens per consumer-warp slice (one per lane). With 128-token tiles this
@@ -332,10 +337,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
           const int64_t t0 = (int64_t)lt * TILE;
           uint32_t bytes = TILE * p.nb;
           if (p.vfmt == SS_V_F16) bytes += TILE * D * 2;
-          else {
-            bytes += TILE * p.v_words * 4 + TILE * p.v_groups * (p.vs_dt == SS_F32 ? 4 : 2);
-            if (p.vz) bytes += TILE * p.v_groups * 4;
-          }
+          else bytes += p.v_tile_bytes;
           if (p.n_heavy) bytes += TILE * p.n_heavy * p.bd * 2;
           mbar_arrive_expect_tx(&full_bar[s], bytes);
           bulk_g2s(st + p.off_idx, p.idx + pair * p.idx_ps + t0 * p.nb, TILE * p.nb,
@@ -345,6 +347,9 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
             for (int bx = 0; bx < D / 64; ++bx)
               tma_load_3d(st + bx * TILE * 128, &map_v, bx * 64, static_cast<int32_t>(t0),
                           static_cast<int32_t>(pair), &full_bar[s]);
+          } else if (p.vfmt == SS_V_VQ) {
+            bulk_g2s(aux, p.vidx + pair * p.vi_ps + t0 * p.v_nb, TILE * p.v_nb, &full_bar[s]);
+            aux += TILE * p.v_nb;
           } else {
             const uint32_t wb = TILE * p.v_words * 4;
             bulk_g2s(aux, p.vq + pair * p.vq_ps + t0 * p.v_words, wb, &full_bar[s]);
@@ -425,17 +430,33 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
   // accuracy); the 16x8 fp32 results go back to one token per lane through
   // the warp's P slice, which is free between P.V and the next softmax.
   const int hd = p.n_heavy * p.bd;
-  uint32_t heavy_off = p.off_aux;
-  if (p.vfmt != SS_V_F16) {
-    heavy_off += TILE * p.v_words * 4 + TILE * p.v_groups * (p.vs_dt == SS_F32 ? 4 : 2);
-    if (p.vz) heavy_off += TILE * p.v_groups * 4;
-  }
+  const uint32_t heavy_off = p.off_aux + (p.vfmt == SS_V_F16 ? 0u : p.v_tile_bytes);
   const bool heavy_mma_shape = HV && (R == 4 || R == 8) && SL == 32 && p.n_heavy > 0 &&
                                hd % 16 == 0 && hd <= 64 && (heavy_off & 15u) == 0;
   // B fragments [k-step][hi, lo][lane] (b0, b1), kept in the codec-query rows
   // once those are built into fragments (nothing else reads them then)
   const uint2* hqs = reinterpret_cast<const uint2*>(&ms.qc[0][0]);
   bool heavy_mma = false;
+
+  if (p.vfmt == SS_V_VQ) {
+    // value centroids, once per CTA: [v_nb][256][v_bd] fp16 with entries
+    // c >= v_k zeroed, so any stored index byte reads a finite row (the
+    // unit loop's first barrier publishes the table)
+    uint16_t* vt = reinterpret_cast<uint16_t*>(smem + p.off_vtab);
+    for (int cid = ctid; cid < p.v_nb * 256; cid += CW * 32) {
+      const int b = cid >> 8, c = cid & 255;
+      const bool ok = c < p.v_k;
+      const uint16_t* src = p.vcents + ((size_t)b * p.v_k + c) * p.v_bd;
+      uint16_t* dst = vt + (size_t)cid * p.v_bd;
+      if (p.v_bd == 4) {
+        *reinterpret_cast<uint2*>(dst) = ok ? __ldg(reinterpret_cast<const uint2*>(src)) : make_uint2(0, 0);
+      } else {
+        for (int j = 0; j < p.v_bd; j += 8)
+          *reinterpret_cast<uint4*>(dst + j) =
+              ok ? __ldg(reinterpret_cast<const uint4*>(src + j)) : make_uint4(0, 0, 0, 0);
+      }
+    }
+  }
 
   int64_t tau = t_begin;
   uint32_t unit_no = 0;
@@ -790,7 +811,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
         const uint32_t vb = smem_u32(vdq_w) + kk_off * 128;
         for (int ks = 0; ks < SL / 16; ++ks) {
           // decode 16 tokens of the slice into this warp's fp16 staging tile
-          if (compressed && D == 128 && p.v_bits == 2 && p.v_group % 16 == 0) {
+          if (compressed && p.vfmt == SS_V_QUANT && D == 128 && p.v_bits == 2 && p.v_group % 16 == 0) {
             // 2-bit codes: lane = (token, half row); four 16-value words per
             // lane in one 16-byte load, one nibble -> two levels per lookup
             const uint8_t* sp = st + p.off_aux + TILE * p.v_words * 4;
@@ -821,6 +842,50 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
                   make_uint4(h[0], h[1], h[2], h[3]);
               *reinterpret_cast<uint4*>(vdq_w + vtile_addr(0, 16, tk, w * 16 + 8)) =
                   make_uint4(h[4], h[5], h[6], h[7]);
+            }
+          } else if (compressed && p.vfmt == SS_V_VQ) {
+            // block-VQ values: lane = (token, half row); one index byte per
+            // block, one table row of v_bd fp16 per block
+            const int tk = lane >> 1, hw = lane & 1;
+            const int tt = slice * SL + ks * 16 + tk;
+            const uint8_t* ir = st + p.off_aux + tt * p.v_nb;
+            const uint16_t* vt = reinterpret_cast<const uint16_t*>(smem + p.off_vtab);
+            if (p.v_bd == 4) {
+              const uint4 c4 = *reinterpret_cast<const uint4*>(ir + hw * 16);
+              const uint32_t cw4[4] = {c4.x, c4.y, c4.z, c4.w};
+#pragma unroll
+              for (int w = 0; w < 4; ++w) {
+#pragma unroll
+                for (int j = 0; j < 4; j += 2) {
+                  const int b = hw * 16 + w * 4 + j;
+                  const uint32_t c0 = (cw4[w] >> (8 * j)) & 255u, c1 = (cw4[w] >> (8 * j + 8)) & 255u;
+                  const uint2 e0 = *reinterpret_cast<const uint2*>(vt + ((b << 8) + c0) * 4);
+                  const uint2 e1 = *reinterpret_cast<const uint2*>(vt + (((b + 1) << 8) + c1) * 4);
+                  *reinterpret_cast<uint4*>(vdq_w + vtile_addr(0, 16, tk, b * 4)) =
+                      make_uint4(e0.x, e0.y, e1.x, e1.y);
+                }
+              }
+            } else if (p.v_bd == 8) {
+              const uint2 c2 = *reinterpret_cast<const uint2*>(ir + hw * 8);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const int b = hw * 8 + j;
+                const uint32_t c = ((j < 4 ? c2.x : c2.y) >> (8 * (j & 3))) & 255u;
+                *reinterpret_cast<uint4*>(vdq_w + vtile_addr(0, 16, tk, b * 8)) =
+                    *reinterpret_cast<const uint4*>(vt + ((b << 8) + c) * 8);
+              }
+            } else {
+              const uint32_t c1 = *reinterpret_cast<const uint32_t*>(ir + hw * 4);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const int b = hw * 4 + j;
+                const uint32_t c = (c1 >> (8 * j)) & 255u;
+                const uint16_t* e = vt + ((b << 8) + c) * 16;
+                *reinterpret_cast<uint4*>(vdq_w + vtile_addr(0, 16, tk, b * 16)) =
+                    *reinterpret_cast<const uint4*>(e);
+                *reinterpret_cast<uint4*>(vdq_w + vtile_addr(0, 16, tk, b * 16 + 8)) =
+                    *reinterpret_cast<const uint4*>(e + 8);
+              }
             }
           } else if (compressed) {
             const uint32_t* words = reinterpret_cast<const uint32_t*>(st + p.off_aux);
@@ -1046,7 +1111,7 @@ __global__ void lse_merge_kernel(const float* parts, int n_parts, int64_t rows, 
 struct Plan {
   int R, cw, tile, n_rg, n_ct, n_tt, tpu, grid, stages, max_cov, v_words, v_groups;
   int64_t total_tiles, n_units;
-  uint32_t stage_bytes, off_idx, off_aux, off_vdq, off_lut, off_p, off_misc;
+  uint32_t stage_bytes, off_idx, off_aux, off_vdq, off_lut, off_p, off_misc, off_vtab, v_tile_bytes;
   size_t smem;
   size_t ws_bytes, off_counters, off_slots, off_lut_g, lut_unit_bytes;
 };
@@ -1061,7 +1126,12 @@ int make_plan_r(const ss_decode_args* a, Plan& pl, int r_cap, int cw) {
   SS_REQUIRE(a->hkv > 0 && a->hq % a->hkv == 0, "ss_decode_attn: hq must be a multiple of hkv");
   SS_REQUIRE(a->b >= 0 && a->tq >= 1 && a->tc >= 0 && a->ttail >= 0,
              "ss_decode_attn: bad batch / lengths");
-  SS_REQUIRE(a->vfmt == SS_V_F16 || a->vfmt == SS_V_QUANT, "ss_decode_attn: bad vfmt");
+  SS_REQUIRE(a->vfmt == SS_V_F16 || a->vfmt == SS_V_QUANT || a->vfmt == SS_V_VQ,
+             "ss_decode_attn: bad vfmt");
+  if (a->vfmt == SS_V_VQ)
+    SS_REQUIRE(a->d == 128 && (a->v_bd == 4 || a->v_bd == 8 || a->v_bd == 16) && a->v_k >= 1 &&
+                   a->v_k <= 256,
+               "ss_decode_attn: VQ values need head_dim 128, v_bd in {4, 8, 16}, v_k <= 256");
   SS_REQUIRE(a->n_heavy >= 0 && a->n_heavy <= 32, "ss_decode_attn: n_heavy must be <= 32");
   const int nb = a->d / a->bd;
   const int nrep = a->hq / a->hkv;
@@ -1105,19 +1175,24 @@ int make_plan_r(const ss_decode_args* a, Plan& pl, int r_cap, int cw) {
   if (a->vfmt == SS_V_QUANT) {
     aux += T * pl.v_words * 4 + T * pl.v_groups * sbytes;
     if (a->v_zeros) aux += T * pl.v_groups * 4;
+  } else if (a->vfmt == SS_V_VQ) {
+    aux += T * (a->d / a->v_bd);
   }
+  pl.v_tile_bytes = aux;
   aux += T * a->n_heavy * a->bd * 2;
   pl.stage_bytes = (pl.off_aux + aux + 1023) & ~1023u;
   size_t fixed = 0;
   // per-warp fp16 value slices (16 tokens) for the quantized path
-  const size_t vdq = (a->vfmt == SS_V_QUANT) ? (size_t)cw * 16 * a->d * 2 : 0;
+  const size_t vdq = (a->vfmt != SS_V_F16) ? (size_t)cw * 16 * a->d * 2 : 0;
+  // VQ value centroids [nb_v][256][bd_v] fp16, resident for the whole launch
+  const size_t vtab = (a->vfmt == SS_V_VQ) ? (size_t)a->d * 256 * 2 : 0;
   // the LUT region doubles as the per-warp merge scratch at unit ends
   size_t lut = (size_t)nb * a->k * R * 4;
   // per-warp merge scratch + the merged rows of the unit
   const size_t scratch = (size_t)cw * R * (a->d + 2) * 4 + (size_t)R * a->d * 4;
   if (lut < scratch) lut = scratch;
   const size_t pbytes = (size_t)cw * slice_tokens(R) * 16;  // per-warp P slice [tokens][8] fp16
-  fixed = vdq + ((lut + 127) & ~size_t(127)) + pbytes + ((sizeof(Misc) + 127) & ~size_t(127)) + 1024;
+  fixed = vdq + vtab + ((lut + 127) & ~size_t(127)) + pbytes + ((sizeof(Misc) + 127) & ~size_t(127)) + 1024;
   if (fixed + 2 * (size_t)pl.stage_bytes > kSmemBudget)
     return fail(SS_ERR_UNSUPPORTED, "ss_decode_attn: configuration exceeds shared memory");
   int stages = static_cast<int>((kSmemBudget - fixed) / pl.stage_bytes);
@@ -1135,6 +1210,8 @@ int make_plan_r(const ss_decode_args* a, Plan& pl, int r_cap, int cw) {
   size_t off = (size_t)stages * pl.stage_bytes;
   pl.off_vdq = static_cast<uint32_t>(off);
   off += vdq;
+  pl.off_vtab = static_cast<uint32_t>(off);
+  off += vtab;
   pl.off_lut = static_cast<uint32_t>(off);
   off += (lut + 127) & ~size_t(127);
   pl.off_p = static_cast<uint32_t>(off);
@@ -1153,18 +1230,20 @@ int make_plan_r(const ss_decode_args* a, Plan& pl, int r_cap, int cw) {
 }
 
 // Largest row group that fits: 8 query rows per unit need a 128 KB table next
-// to the stage ring; when that does not fit (wide stages, e.g. heavy key
-// blocks) the rows are split into groups of 4, which streams the unit twice.
+// to the stage ring; when that does not fit (wide stages, or the value
+// centroid table of VQ values) the rows are split into smaller groups, each of
+// which streams the unit once.
 // 12 consumer warps (more latency hiding for the table gather) when six
 // stages fit, i.e. for compact value formats; 8 warps with 4 stages otherwise.
 int make_plan(const ss_decode_args* a, Plan& pl) {
   int rc = SS_ERR_UNSUPPORTED;
-  for (int r_cap : {8, 4}) {
+  for (int r_cap = 8;;) {
     for (int cw : {12, 8}) {
       rc = make_plan_r(a, pl, r_cap, cw);
       if (rc != SS_ERR_UNSUPPORTED) return rc;
     }
-    if (pl.R != 8) break;  // a smaller row group cannot help
+    if (pl.R <= 1) break;
+    r_cap = pl.R / 2;  // halve the row group (the stream is read once per group)
   }
   return rc;
 }
@@ -1229,6 +1308,8 @@ int run_decode(const ss_decode_args* a, float* part_out, void* stream) {
   SS_REQUIRE(a->tc == 0 || a->vfmt != SS_V_F16 || a->v, "ss_decode_attn: v is null");
   SS_REQUIRE(a->tc == 0 || a->vfmt != SS_V_QUANT || (a->vq && a->v_scales),
              "ss_decode_attn: quantized values are null");
+  SS_REQUIRE(a->tc == 0 || a->vfmt != SS_V_VQ || (a->v_idx && a->v_cents),
+             "ss_decode_attn: VQ value indices / centroids are null");
   cudaStream_t st = as_stream(stream);
   const int64_t n_pairs = (int64_t)a->b * a->hkv;
   if (pl.total_tiles == 0 || n_pairs == 0) return SS_OK;  // caller zero-fills empty caches
@@ -1249,6 +1330,12 @@ int run_decode(const ss_decode_args* a, float* part_out, void* stream) {
                      aligned(a->v_scales, a->vs_pair_stride * sb) &&
                      (!a->v_zeros || aligned(a->v_zeros, a->vz_pair_stride * 4)),
                  "ss_decode_attn: quantized value streams must be 16-byte aligned");
+    }
+    if (a->vfmt == SS_V_VQ) {
+      SS_REQUIRE(aligned(a->v_idx, a->vi_pair_stride) && aligned(a->v_cents, 0),
+                 "ss_decode_attn: VQ value indices / centroids must be 16-byte aligned");
+      SS_REQUIRE(a->vi_pair_stride / (a->d / a->v_bd) >= (int64_t)pl.n_ct * pl.tile,
+                 "ss_decode_attn: VQ value rows per pair must cover whole 128-token tiles");
     }
     if (a->n_heavy)
       SS_REQUIRE(aligned(a->kheavy, a->kheavy_pair_stride * 2),
@@ -1294,6 +1381,9 @@ int run_decode(const ss_decode_args* a, float* part_out, void* stream) {
   p.vz = a->v_zeros; p.vz_ps = a->vz_pair_stride;
   for (int i = 0; i < 16; ++i) p.levels[i] = a->v_levels[i];
   p.v_rot = a->v_rot;
+  p.vidx = a->v_idx; p.vi_ps = a->vi_pair_stride; p.vcents = a->v_cents;
+  p.v_bd = a->v_bd; p.v_k = a->v_k; p.v_nb = a->v_bd > 0 ? a->d / a->v_bd : 0;
+  p.v_tile_bytes = pl.v_tile_bytes; p.off_vtab = pl.off_vtab;
   p.k_tail = a->k_tail; p.v_tail = a->v_tail; p.tail_ps = a->tail_pair_stride;
   p.causal = a->causal; p.mask = a->mask; p.mask_stride = a->mask_stride;
   p.mask_mode = a->mask_mode;

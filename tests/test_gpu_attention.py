@@ -264,6 +264,42 @@ def test_heavy_block_scoring_shapes(ss, n_heavy, hq, qdt, vals):
     assert G.rel_err(out, want) < tol, G.rel_err(out, want)
 
 
+@pytest.mark.parametrize("vbd,vmode,buf,tq", [
+    (4, "profileperm_baseline", 0, 1), (8, "profileperm_baseline", 32, 1),
+    (16, "profileperm_baseline", 0, 1), (4, "rotated", 16, 1),
+    (8, "rotated", 0, 1), (4, "profileperm_baseline", 16, 5)])
+def test_vq_values_fused_decode(ss, vbd, vmode, buf, tq):
+    """value_backend="sunshape" (cache.py:785-812): block-VQ value indices
+    decoded inside the fused kernel from an fp16 centroid table, accumulated
+    in the value codec's basis and transformed back once; compared with the
+    reference semantics softmax(q k_hat^T) v_hat, v_hat = fp16(dequantize(v))."""
+    rng = np.random.default_rng(60 + vbd + 3 * buf + tq + len(vmode))
+    kc = rng.standard_normal((2048, 128)).astype(np.float32)
+    qc = rng.standard_normal((1024, 128)).astype(np.float32)
+    kcodec = ss.SunShapeBlockCodec(head_dim=128, block_dim=4)
+    kcodec.fit(qc, kc, kmeans_iters=3, seed=0)
+    vcal = rng.standard_normal((2048, 128)).astype(np.float32)
+    vcodec = ss.SunShapeBlockCodec(head_dim=128, block_dim=vbd, mode=vmode)
+    vcodec.fit(qc, vcal, kmeans_iters=3, seed=1)
+    cache = ss.create_kv_cache(kcodec, n_kv_heads=2, value_backend="sunshape", value_bits=8,
+                               value_codec=vcodec, buffer_size=buf)
+    kk, vv = I.kv_stream(21, 2, 2, 777, 128)
+    cache.update_and_fetch(kk, vv)
+    q = torch.tensor(I.decode_queries(22, 2, 8, tq, 128), device="cuda")
+    out = ss.sunshape_sdpa(q, cache, 1 / math.sqrt(128), mask="causal" if tq > 1 else None)
+    kt = torch.tensor(kk, device="cuda")
+    vt = torch.tensor(vv, device="cuda")
+    c = 777 - buf
+    khat = torch.cat([torch.stack([torch.stack([kcodec(kt[b, h, :c]) for h in range(2)]) for b in range(2)]),
+                      kt[:, :, c:].half().float()], 2)
+    vhat = torch.cat([torch.stack([torch.stack([vcodec(vt[b, h, :c]) for h in range(2)]) for b in range(2)]).half(),
+                      vt[:, :, c:].half()], 2)
+    want = G.attention(G.scaled_queries(q, 1 / math.sqrt(128)), khat, vhat.float(), causal=tq > 1)
+    assert G.rel_err(out, want) < 2e-3, G.rel_err(out, want)
+    # the cache's decoded values agree with the codec (the unfused view)
+    torch.testing.assert_close(cache.values[:, :, :c].float(), vhat[:, :, :c].float())
+
+
 def test_empty_cache_returns_zeros(ss, cfg1_codec):
     cache = ss.create_kv_cache(cfg1_codec, n_kv_heads=2)
     q = torch.randn((1, 4, 1, 128), device="cuda").half()
