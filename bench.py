@@ -244,19 +244,22 @@ def run_ours(args, world, rank, local):
     # ---- e2e through the public API with host buffers
     e2e = None
     if not args.no_e2e:
-        qh = q.cpu().pin_memory()
+        # one pinned staging buffer per step holding the query and the new
+        # K/V token, copied to the device in one transfer
         g = torch.Generator().manual_seed(99 + rank)
-        kh = torch.randn((B, HKV, 1, D), generator=g).half().pin_memory()
-        vh = torch.randn((B, HKV, 1, D), generator=g).half().pin_memory()
+        nq, nkv = q.numel(), B * HKV * D
+        hin = torch.empty(nq + 2 * nkv, dtype=torch.float16).pin_memory()
+        hin[:nq] = q.cpu().reshape(-1)
+        hin[nq:] = torch.randn(2 * nkv, generator=g).half()
+        qh, kh, vh = hin[:nq], hin[nq:nq + nkv], hin[nq + nkv:]
         oh = torch.empty((B, HQ, 1, D), dtype=torch.float16).pin_memory()
-        qd = torch.empty_like(q)
-        kd = torch.empty((B, HKV, 1, D), dtype=torch.float16, device=device)
-        vd = torch.empty_like(kd)
+        din = torch.empty(hin.numel(), dtype=torch.float16, device=device)
+        qd = din[:nq].view(B, HQ, 1, D)
+        kd = din[nq:nq + nkv].view(B, HKV, 1, D)
+        vd = din[nq + nkv:].view(B, HKV, 1, D)
 
         def e2e_step():
-            qd.copy_(qh, non_blocking=True)
-            kd.copy_(kh, non_blocking=True)
-            vd.copy_(vh, non_blocking=True)
+            din.copy_(hin, non_blocking=True)
             cache.append(kd, vd)
             out = ss.sunshape_sdpa(qd, cache, scale)
             oh.copy_(out, non_blocking=True)

@@ -83,6 +83,27 @@ int ss_vq_assign(const void* keys, int key_dtype, int64_t n_groups, int64_t rows
                  int64_t idx_row_stride, uint16_t* out_heavy, int64_t heavy_group_stride,
                  int64_t heavy_row_stride, float* out_pt, int dist_mode, void* stream);
 
+/* ----------------------------------------------------------------------------
+ * Cache append (the write half of update_and_fetch, cache.py:156-205): new
+ * keys are quantized as ss_vq_assign (dist_mode 0) into the index stream at
+ * the write position (heavy blocks into kheavy when given), and the new
+ * values are stored as f16 rows. Rows: n_groups groups (batch x kv-head) of
+ * `rows` new tokens; destination pointers already point at the write
+ * position. Decode-sized appends (<= 4096 rows) are one launch.
+ * -------------------------------------------------------------------------- */
+typedef struct ss_append_args {
+  const void* keys; int key_dtype; int64_t key_group_stride, key_row_stride;
+  const void* values; int value_dtype; int64_t value_group_stride, value_row_stride;
+  int64_t n_groups, rows;
+  int d;
+  const int32_t* perm; const float* centroids; int bd, k; const uint8_t* heavy;
+  uint8_t* idx; int64_t idx_group_stride, idx_row_stride;
+  uint16_t* kheavy; int64_t kheavy_group_stride, kheavy_row_stride;
+  uint16_t* v; int64_t v_group_stride, v_row_stride;
+} ss_append_args;
+
+int ss_cache_append(const ss_append_args* a, void* stream);
+
 /* Assignment kernel selection (no counterpart in the reference, which has one
  * CPU loop and one Metal kernel): 0 = automatic (tensor-core kernel for
  * >= 16384 rows when bd in {4,8,16}, k in {64,128,192,256}, d <= 128 and key rows are

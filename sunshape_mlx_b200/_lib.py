@@ -73,6 +73,22 @@ class DecodeArgs(C.Structure):
     ]
 
 
+class AppendArgs(C.Structure):
+    """Mirror of ss_append_args."""
+
+    _fields_ = [
+        ("keys", vp), ("key_dtype", i32), ("key_group_stride", i64), ("key_row_stride", i64),
+        ("values", vp), ("value_dtype", i32), ("value_group_stride", i64),
+        ("value_row_stride", i64),
+        ("n_groups", i64), ("rows", i64),
+        ("d", i32),
+        ("perm", vp), ("centroids", vp), ("bd", i32), ("k", i32), ("heavy", vp),
+        ("idx", vp), ("idx_group_stride", i64), ("idx_row_stride", i64),
+        ("kheavy", vp), ("kheavy_group_stride", i64), ("kheavy_row_stride", i64),
+        ("v", vp), ("v_group_stride", i64), ("v_row_stride", i64),
+    ]
+
+
 _SIGS = {
     "ss_abi_version": ([], i32),
     "ss_last_error": ([], C.c_char_p),
@@ -97,6 +113,7 @@ _SIGS = {
                          vp, i32, i64, i64, vp], i32),
     "ss_decode_workspace_size": ([C.POINTER(DecodeArgs)], C.c_size_t),
     "ss_decode_attn": ([C.POINTER(DecodeArgs), vp], i32),
+    "ss_cache_append": ([C.POINTER(AppendArgs), vp], i32),
     "ss_decode_attn_partial": ([C.POINTER(DecodeArgs), vp, vp], i32),
     "ss_decode_check": ([vp, vp], i32),
     "ss_set_assign_path": ([i32], i32),

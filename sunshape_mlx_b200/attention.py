@@ -220,20 +220,31 @@ def _sdpa_simple_fast(q: torch.Tensor, cache, scale: float) -> torch.Tensor:
                              codec.heavy_u8, n_heavy)
         keep += [spec, rot_k]
         lib = L.load()
-        memo = (key, a, keep, lib, C.byref(a))
+        memo = (key, a, keep, lib, C.byref(a), {})
         cache._sdpa_memo = memo
-    _, a, _, lib, ref = memo
+    _, a, _, lib, ref, ws_by_tiles = memo
     out = torch.empty_like(q)
     a.q = q.data_ptr()
     a.out = out.data_ptr()
     a.tc = cache.offset
-    nbytes = lib.ss_decode_workspace_size(ref)
-    if nbytes == 0:
-        raise L.SunShapeCudaError("ss_decode_workspace_size", 1, L.last_error())
-    ws = workspace_for(q.device, nbytes)
+    # the workspace size depends on the token count only through its tiles;
+    # workspaces belong to a stream
+    sp = torch.cuda.current_stream(q.device).cuda_stream
+    tiles = ((cache.offset + 127) >> 7, sp)
+    ws = ws_by_tiles.get(tiles)
+    if ws is None:
+        nbytes = lib.ss_decode_workspace_size(ref)
+        if nbytes == 0:
+            raise L.SunShapeCudaError("ss_decode_workspace_size", 1, L.last_error())
+        ws = workspace_for(q.device, nbytes)
+        if len(ws_by_tiles) > 64:
+            ws_by_tiles.clear()
+        ws_by_tiles[tiles] = ws
     a.workspace = ws.data_ptr()
     a.workspace_bytes = ws.numel()
-    L.check("ss_decode_attn", lib.ss_decode_attn(ref, L.stream_ptr(q.device)))
+    rc = lib.ss_decode_attn(ref, C.c_void_p(sp))
+    if rc:
+        L.check("ss_decode_attn", rc)
     codec.last_score_backend = "cuda_fused"
     return out
 

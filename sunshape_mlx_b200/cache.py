@@ -113,41 +113,58 @@ class SunShapeKVCache:
             return
         self._ensure_capacity(B, T)
         o = self.offset
-        if not self._assign_fast(k, o):
+        if not self._append_fast(k, v, o):
             _quantize_keys_into(self.codec, k, self._key_indices[:, :, o:o + T],
                                 None if self._key_heavy is None else self._key_heavy[:, :, o:o + T])
-        self._values.narrow(2, o, T).copy_(v)
+            self._values.narrow(2, o, T).copy_(v)
         self.offset += T
 
-    def _assign_fast(self, k: torch.Tensor, o: int) -> bool:
-        """ss_vq_assign straight into the index stream at token o, with the
-        arguments that only change on reallocation kept from the last call
-        (the per-token decode append is otherwise dominated by host work)."""
+    def _append_fast(self, k: torch.Tensor, v: torch.Tensor, o: int) -> bool:
+        """ss_cache_append: keys quantized into the index stream and values
+        stored at token o in one launch, with an argument block kept from the
+        last call (rebuilt on reallocation or a layout change), so a decode
+        step's append is one short C call."""
         codec = self.codec
         B, H, T, D = k.shape
-        if codec.use_rotation or k.stride(3) != 1 or k.stride(0) != H * k.stride(1):
+        if (codec.use_rotation or k.stride(3) != 1 or k.stride(0) != H * k.stride(1)
+                or v.shape != k.shape or v.stride(3) != 1 or v.stride(0) != H * v.stride(1)):
             return False
-        key = (self._epoch, k.dtype, k.stride(1), k.stride(2), codec.centroids.data_ptr(),
-               codec.permutation.data_ptr(), codec._is_perm(), codec.n_heavy_blocks)
+        key = (self._epoch, k.dtype, k.stride(1), k.stride(2), v.dtype, v.stride(1), v.stride(2),
+               codec.centroids.data_ptr(), codec.permutation.data_ptr(), codec._is_perm(),
+               codec.n_heavy_blocks)
         memo = self._assign_memo
         if memo is None or memo[0] != key:
             L = K.L
+            a = L.AppendArgs()
+            a.key_dtype, a.key_group_stride, a.key_row_stride = L.dtype_code(k.dtype), k.stride(1), k.stride(2)
+            a.value_dtype, a.value_group_stride, a.value_row_stride = L.dtype_code(v.dtype), v.stride(1), v.stride(2)
+            a.n_groups, a.d = B * H, D
             perm = codec.permutation if codec._is_perm() else None
-            ki, kh = self._key_indices, self._key_heavy
-            memo = (key, L.load().ss_vq_assign, L.dtype_code(k.dtype), B * H, k.stride(1),
-                    k.stride(2), D, L.ptr(perm), L.ptr(codec.centroids), codec.block_dim,
-                    codec.n_centroids, L.ptr(codec.heavy_u8), ki.data_ptr(), ki.stride(1),
-                    ki.stride(2), None if kh is None else kh.data_ptr(),
-                    0 if kh is None else kh.stride(1), 0 if kh is None else kh.stride(2),
-                    codec)
+            a.perm = L.ptr(perm)
+            a.centroids = L.ptr(codec.centroids)
+            a.bd, a.k = codec.block_dim, codec.n_centroids
+            a.heavy = L.ptr(codec.heavy_u8)
+            ki, kh, vv = self._key_indices, self._key_heavy, self._values
+            a.idx_group_stride, a.idx_row_stride = ki.stride(1), ki.stride(2)
+            if kh is not None:
+                a.kheavy_group_stride, a.kheavy_row_stride = kh.stride(1), kh.stride(2)
+            a.v_group_stride, a.v_row_stride = vv.stride(1), vv.stride(2)
+            bases = (ki.data_ptr(), None if kh is None else kh.data_ptr(), vv.data_ptr())
+            memo = (key, a, L.C.byref(a), L.load().ss_cache_append, bases,
+                    (ki.stride(2), 0 if kh is None else 2 * kh.stride(2), 2 * vv.stride(2)),
+                    [codec, perm])
             self._assign_memo = memo
-        (_, fn, dt, g, kgs, krs, d, perm_p, cents_p, bd, kc, heavy_p, ki_p, igs, irs, kh_p, hgs,
-         hrs, _) = memo
-        rc = fn(K.L.C.c_void_p(k.data_ptr()), dt, g, T, kgs, krs, d, perm_p, cents_p, bd, kc,
-                heavy_p, K.L.C.c_void_p(ki_p + o * irs), igs, irs,
-                None if kh_p is None else K.L.C.c_void_p(kh_p + 2 * o * hrs), hgs, hrs, None, 0,
-                K.L.stream_ptr(self.device))
-        K.L.check("ss_vq_assign", rc)
+        _, a, ref, fn, (ki_p, kh_p, v_p), (irs, hrs2, vrs2), _ = memo
+        a.keys = k.data_ptr()
+        a.values = v.data_ptr()
+        a.rows = T
+        a.idx = ki_p + o * irs
+        if kh_p is not None:
+            a.kheavy = kh_p + o * hrs2
+        a.v = v_p + o * vrs2
+        rc = fn(ref, K.L.stream_ptr(self.device))
+        if rc:
+            K.L.check("ss_cache_append", rc)
         return True
 
     def update_and_fetch(self, keys, values):

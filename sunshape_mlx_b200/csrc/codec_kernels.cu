@@ -31,7 +31,31 @@ struct AssignParams {
   float* out_pt;
   int dist_mode;
   int b_per_cta;  // blocks handled by one CTA (grid.y = ceil(nb / b_per_cta))
+  // optional value rows copied (as f16) next to the keys: a cache append
+  const void* vsrc;
+  int vdt;
+  int64_t vgs, vrs;
+  uint16_t* vdst;
+  int64_t vdgs, vdrs;
 };
+
+// Value rows of a cache append: rows [r0, r0 + n) of the (group, row) space,
+// d elements each, converted to f16 (the cache's value dtype).
+__device__ __forceinline__ void copy_value_rows(const AssignParams& p, int64_t r0, int n,
+                                                int tid, int nthr) {
+  const int64_t n_rows = p.n_groups * p.rpg;
+  for (int e = tid; e < n * p.d; e += nthr) {
+    const int rr = e / p.d, j = e - rr * p.d;
+    const int64_t r = r0 + rr;
+    if (r >= n_rows) continue;
+    const int64_t g = r / p.rpg, t = r - g * p.rpg;
+    p.vdst[g * p.vdgs + t * p.vdrs + j] = f2h(load_as_f32(p.vsrc, p.vdt, g * p.vgs + t * p.vrs + j));
+  }
+}
+
+__global__ void __launch_bounds__(256) copy_value_rows_kernel(AssignParams p) {
+  copy_value_rows(p, (int64_t)blockIdx.x * 32, 32, threadIdx.x, 256);
+}
 
 template <int BD>
 __global__ void __launch_bounds__(kAssignThreads) vq_assign_kernel(AssignParams p) {
@@ -158,6 +182,8 @@ __global__ void __launch_bounds__(kAssignThreads) vq_assign_small_kernel(AssignP
   __shared__ float s_d0[32];
   const int b = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (p.vdst && b == 0) copy_value_rows(p, (int64_t)blockIdx.x * kAssignRows, kAssignRows, tid,
+                                        kAssignThreads);
   const int64_t n_rows = p.n_groups * p.rpg;
   const int64_t r = (int64_t)blockIdx.x * kAssignRows + lane;
   const bool valid = r < n_rows;
@@ -477,6 +503,51 @@ int ss_vq_assign(const void* keys, int key_dtype, int64_t n_groups, int64_t rows
   }
 #undef SS_LAUNCH_ASSIGN
   return check_launch("ss_vq_assign");
+}
+
+int ss_cache_append(const ss_append_args* a, void* stream) {
+  SS_REQUIRE(a && a->keys && a->values && a->idx && a->v && a->centroids,
+             "ss_cache_append: null pointer");
+  SS_REQUIRE(a->value_dtype >= SS_F32 && a->value_dtype <= SS_BF16,
+             "ss_cache_append: bad value dtype");
+  const int64_t rows = a->n_groups * a->rows;
+  if (a->n_groups <= 0 || a->rows <= 0) return SS_OK;
+  const bool small = rows <= kSmallRows && g_assign_path != 2 &&
+                     (a->bd == 2 || a->bd == 4 || a->bd == 8 || a->bd == 16);
+  if (!small) {
+    // bulk append (prefill): the assignment dispatch of ss_vq_assign, then the value rows
+    const int rc = ss_vq_assign(a->keys, a->key_dtype, a->n_groups, a->rows, a->key_group_stride,
+                                a->key_row_stride, a->d, a->perm, a->centroids, a->bd, a->k,
+                                a->heavy, a->idx, a->idx_group_stride, a->idx_row_stride,
+                                a->kheavy, a->kheavy_group_stride, a->kheavy_row_stride, nullptr,
+                                0, stream);
+    if (rc != SS_OK) return rc;
+  }
+  SS_REQUIRE(a->d > 0 && a->d <= 1024 && a->d % a->bd == 0 && a->d / a->bd <= 128,
+             "ss_cache_append: bad d / bd");
+  SS_REQUIRE(a->k >= 1 && a->k <= 256, "ss_cache_append: k must be in [1, 256]");
+  SS_REQUIRE(a->key_dtype >= SS_F32 && a->key_dtype <= SS_BF16, "ss_cache_append: bad key dtype");
+  AssignParams p{a->keys, a->key_dtype, a->n_groups, a->rows, a->key_group_stride,
+                 a->key_row_stride, a->d, a->d / a->bd, a->k, a->perm, a->centroids, a->heavy,
+                 a->idx, a->idx_group_stride, a->idx_row_stride, a->kheavy,
+                 a->kheavy_group_stride, a->kheavy_row_stride, nullptr, 0, 0,
+                 a->values, a->value_dtype, a->value_group_stride, a->value_row_stride, a->v,
+                 a->v_group_stride, a->v_row_stride};
+  cudaStream_t st = as_stream(stream);
+  const unsigned tiles = static_cast<unsigned>((rows + kAssignRows - 1) / kAssignRows);
+  if (!small) {
+    copy_value_rows_kernel<<<tiles, 256, 0, st>>>(p);
+    return check_launch("ss_cache_append (values)");
+  }
+  count_dispatch("ss_cache_append");
+  const dim3 grid_s(tiles, static_cast<unsigned>(p.nb));
+  switch (a->bd) {
+    case 2: vq_assign_small_kernel<2><<<grid_s, kAssignThreads, 0, st>>>(p); break;
+    case 4: vq_assign_small_kernel<4><<<grid_s, kAssignThreads, 0, st>>>(p); break;
+    case 8: vq_assign_small_kernel<8><<<grid_s, kAssignThreads, 0, st>>>(p); break;
+    default: vq_assign_small_kernel<16><<<grid_s, kAssignThreads, 0, st>>>(p); break;
+  }
+  return check_launch("ss_cache_append");
 }
 
 int ss_kmeans_update(const float* data, int64_t n, int nb, int bd, const uint8_t* assign,
