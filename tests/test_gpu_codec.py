@@ -201,3 +201,38 @@ def test_block_vq_score_from_table(ss):
     assert np.abs(got - want).max() < 1e-3
     got2 = ss.block_vq_score_metal(qd[:2, :8, :64], idx[:16, :8] % 64, 2, 16, 8, 64)
     assert tuple(got2.shape) == (2, 16)
+
+
+@pytest.mark.parametrize("B,T,heavy,kdt", [(2, 3, False, torch.float16), (1, 40, True, torch.float32),
+                                           (3, 2500, True, torch.float16), (2, 2049, False, torch.bfloat16),
+                                           (4, 2100, False, torch.float16)])
+def test_cache_append_matches_assign_and_values(ss, B, T, heavy, kdt):
+    """ss_cache_append (one launch for decode-sized appends, the assignment
+    dispatch plus a row copy above 4096 rows): indices equal ss_vq_assign's,
+    heavy blocks land in the fp16 stream, values are stored as fp16, and rows
+    outside the write position are untouched."""
+    from sunshape_mlx_b200 import kernels as K
+
+    rng = np.random.default_rng(70 + T)
+    qc = I.heavy_tailed_queries(1024, 128, seed=3)
+    kc = rng.standard_normal((2048, 128)).astype(np.float32)
+    mode = "profileperm_mixed_precision" if heavy else "profileperm_baseline"
+    codec = ss.SunShapeBlockCodec(head_dim=128, mode=mode, **({"n_heavy": 4} if heavy else {}))
+    codec.fit(qc, kc, kmeans_iters=2, seed=0)
+    cache = ss.create_kv_cache(codec, n_kv_heads=2)
+    k0 = torch.tensor(rng.standard_normal((B, 2, 37, 128)), device="cuda").half()
+    cache.append(k0, k0 * 2)
+    k = torch.tensor(rng.standard_normal((B, 2, T, 128)), device="cuda").to(kdt)
+    v = torch.tensor(rng.standard_normal((B, 2, T, 128)), device="cuda").to(kdt)
+    cache.append(k, v)
+    assert cache.offset == 37 + T
+    want = K.vq_assign(k.reshape(B * 2, T, 128), codec.centroids,
+                       perm=codec.permutation, heavy=codec.heavy_u8).reshape(B, 2, T, -1)
+    assert torch.equal(cache._key_indices[:, :, 37:37 + T], want)
+    assert torch.equal(cache._values[:, :, 37:37 + T], v.half())
+    assert torch.equal(cache._values[:, :, :37], (k0 * 2).half())
+    if heavy:
+        hp = torch.nonzero(codec.heavy_u8).flatten().tolist()
+        kp = k.float()[..., codec.permutation.long()].reshape(B, 2, T, -1, 8)
+        assert torch.equal(cache._key_heavy[:, :, 37:37 + T],
+                           kp[:, :, :, hp].reshape(B, 2, T, -1).half())
