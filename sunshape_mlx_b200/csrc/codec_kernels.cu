@@ -53,8 +53,33 @@ __device__ __forceinline__ void copy_value_rows(const AssignParams& p, int64_t r
   }
 }
 
-__global__ void __launch_bounds__(256) copy_value_rows_kernel(AssignParams p) {
+__global__ void __launch_bounds__(256) copy_value_rows_small_kernel(AssignParams p) {
   copy_value_rows(p, (int64_t)blockIdx.x * 32, 32, threadIdx.x, 256);
+}
+
+// Bulk append of value rows: one thread per 8 consecutive elements of a row,
+// one 16-byte load and store when the source is aligned f16.
+__global__ void __launch_bounds__(256) copy_value_rows_kernel(AssignParams p, int vec) {
+  const int per_row = p.d / 8;
+  const int64_t n_rows = p.n_groups * p.rpg;
+  const int64_t gid = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  const int64_t r = gid / per_row;
+  if (r >= n_rows) return;
+  const int j = static_cast<int>(gid - r * per_row) * 8;
+  const int64_t g = r / p.rpg, t = r - g * p.rpg;
+  uint16_t* dst = p.vdst + g * p.vdgs + t * p.vdrs + j;
+  const int64_t so = g * p.vgs + t * p.vrs + j;
+  if (vec) {
+    *reinterpret_cast<uint4*>(dst) = __ldg(reinterpret_cast<const uint4*>(
+        static_cast<const uint16_t*>(p.vsrc) + so));
+    return;
+  }
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    w[i] = (uint32_t)f2h(load_as_f32(p.vsrc, p.vdt, so + 2 * i)) |
+           ((uint32_t)f2h(load_as_f32(p.vsrc, p.vdt, so + 2 * i + 1)) << 16);
+  *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
 template <int BD>
@@ -536,7 +561,16 @@ int ss_cache_append(const ss_append_args* a, void* stream) {
   cudaStream_t st = as_stream(stream);
   const unsigned tiles = static_cast<unsigned>((rows + kAssignRows - 1) / kAssignRows);
   if (!small) {
-    copy_value_rows_kernel<<<tiles, 256, 0, st>>>(p);
+    if (a->d % 8 == 0 && reinterpret_cast<uintptr_t>(a->v) % 16 == 0 &&
+        (a->v_group_stride * 2) % 16 == 0 && (a->v_row_stride * 2) % 16 == 0) {
+      const int es = a->value_dtype == SS_F32 ? 4 : 2;
+      const int vec = a->value_dtype == SS_F16 && reinterpret_cast<uintptr_t>(a->values) % 16 == 0 &&
+                      (a->value_group_stride * es) % 16 == 0 && (a->value_row_stride * es) % 16 == 0;
+      const int64_t n = rows * (a->d / 8);
+      copy_value_rows_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(p, vec);
+    } else {
+      copy_value_rows_small_kernel<<<tiles, 256, 0, st>>>(p);
+    }
     return check_launch("ss_cache_append (values)");
   }
   count_dispatch("ss_cache_append");

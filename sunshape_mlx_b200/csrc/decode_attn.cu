@@ -208,11 +208,93 @@ __global__ void __launch_bounds__(kLutThreads) lut_kernel(const __grid_constant_
   const int rg = static_cast<int>(u - pair * p.n_rg);
   const int bb = static_cast<int>(pair / p.hkv), hh = static_cast<int>(pair % p.hkv);
   grid_launch_dependents();  // let the decode grid start streaming now
+  float* out = p.lut_g + (size_t)u * (p.lut_unit_bytes / 4);
+  if constexpr (BD > 0) {
+    if (p.rot_k == nullptr) {
+      // Identity / permutation codecs: every global load (centroids, the
+      // block's permutation entries, the query rows) is issued up front so the
+      // kernel pays one memory latency, then one barrier.
+      constexpr int TPB = kLutThreads / kLutBlocks;
+      const int b = b0 + tid / TPB, cl = tid % TPB;
+      const bool bok = b < p.nb;
+      const float* cb = p.cents + (size_t)(bok ? b : 0) * p.k * BD;
+      float cv[4][BD];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int c = cl + i * TPB;
+#pragma unroll
+        for (int j = 0; j < BD; j += 4) {
+          float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (bok && c < p.k) v = __ldg(reinterpret_cast<const float4*>(cb + (size_t)c * BD + j));
+          cv[i][j] = v.x; cv[i][j + 1] = v.y; cv[i][j + 2] = v.z; cv[i][j + 3] = v.w;
+        }
+      }
+      int pj[BD];
+#pragma unroll
+      for (int j = 0; j < BD; ++j) {
+        const int col = (bok ? b : 0) * BD + j;
+        pj[j] = p.perm ? __ldg(p.perm + col) : col;
+      }
+      constexpr int QPT = (R * 128 + kLutThreads - 1) / kLutThreads;
+      const float sc = round_to(p.scale, p.qdt);
+      const int rows_valid = p.nrep * p.tq;
+      float qv[QPT];
+#pragma unroll
+      for (int i = 0; i < QPT; ++i) {
+        const int e = tid + i * kLutThreads;
+        const int r = e / p.d, j = e - r * p.d;
+        const int rr = rg * R + r;
+        qv[i] = 0.f;
+        if (e < R * p.d && rr < rows_valid) {
+          const int rep = rr / p.tq, tqi = rr - rep * p.tq;
+          const int qh = hh * p.nrep + rep;
+          qv[i] = load_as_f32(p.q, p.qdt, bb * p.q_sb + qh * p.q_sh + tqi * p.q_st + j);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < QPT; ++i) {
+        const int e = tid + i * kLutThreads;
+        const int r = e / p.d, j = e - r * p.d;
+        if (e < R * p.d) qo[r][j] = round_to(qv[i] * sc, p.qdt);  // attention.py:208
+      }
+      __syncthreads();
+      if (!bok) return;
+      const bool zero = p.n_heavy > 0 && p.heavy && p.heavy[b];
+      float q[R][BD];
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int j = 0; j < BD; ++j) q[r][j] = zero ? 0.f : qo[r][pj[j]];
+      float* ob = out + (size_t)b * p.k * R;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int c = cl + i * TPB;
+        if (c >= p.k) break;
+        float o[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          float acc = 0.f;
+#pragma unroll
+          for (int j = 0; j < BD; ++j) acc = fmaf(q[r][j], cv[i][j], acc);
+          o[r] = acc;
+        }
+        float* dst = ob + (size_t)c * R;
+        if constexpr (R % 4 == 0) {
+#pragma unroll
+          for (int r = 0; r < R; r += 4)
+            *reinterpret_cast<float4*>(dst + r) = make_float4(o[r], o[r + 1], o[r + 2], o[r + 3]);
+        } else {
+#pragma unroll
+          for (int r = 0; r < R; ++r) dst[r] = o[r];
+        }
+      }
+      return;
+    }
+  }
   unit_query_rows(p, qo, rg, bb, hh, tid, kLutThreads);
   __syncthreads();
   unit_codec_rows(p, qo, qc, tid, kLutThreads);
   __syncthreads();
-  float* out = p.lut_g + (size_t)u * (p.lut_unit_bytes / 4);
   if constexpr (BD > 0) {
     const int b = b0 + tid / (kLutThreads / kLutBlocks);
     if (b >= p.nb) return;
