@@ -23,6 +23,7 @@
 //      P(tokens x rows) with mma.m16n8k16 (fp16 in, fp32 accumulate).
 // Quantized values are first decoded (levels * scale + zero) into an fp16
 // tile in the same swizzled layout and then take the same MMA path.
+#include <algorithm>
 #include <cfloat>
 #include <mutex>
 #include <string>
@@ -46,6 +47,7 @@ struct DecodeParams {
   int R, tile, n_rg, n_ct, n_tt, tpu;
   int64_t tc, ttail, total_tiles, n_units;
   int grid, stages, stage_shift, max_cov;  // stages: a multiple of the tile groups
+  int w_unit;                              // schedule cost of a unit boundary, in tiles
   // queries
   const void* q;
   int qdt;
@@ -125,11 +127,32 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
-__device__ __forceinline__ int64_t cta_of(int64_t tile, int64_t total, int grid) {
-  return ((tile + 1) * grid - 1) / total;
+// Static schedule. CTA k owns the tiles [start(k), start(k + 1)) of the
+// (unit, tile) sequence. A tile costs 1 and every unit boundary costs w more
+// (the merge, cross-CTA publish and table reload at a unit end), so ranges
+// are equal in cost c(t) = t + w * floor(t / tpu), not in tiles; a CTA whose
+// range crosses a unit boundary gets about w fewer tiles.
+struct Sched {
+  int64_t total, tpu, w, cost;  // cost = c(total - 1) + 1
+  int grid;
+};
+__host__ __device__ inline Sched make_sched(int64_t total, int64_t tpu, int64_t w, int grid) {
+  Sched s{total, tpu, w, total + w * (total / tpu - 1), grid};
+  return s;
 }
-__device__ __forceinline__ int64_t range_start(int64_t i, int64_t total, int grid) {
-  return i * total / grid;
+// smallest t with c(t) * grid >= k * cost
+__host__ __device__ inline int64_t range_start(const Sched& s, int64_t k) {
+  if (k >= s.grid) return s.total;
+  const int64_t y = k * s.cost;
+  const int64_t pg = (s.tpu + s.w) * s.grid;
+  const int64_t j = y / pg;
+  const int64_t x = (y - j * pg + s.grid - 1) / s.grid;
+  const int64_t t = x < s.tpu ? j * s.tpu + x : (j + 1) * s.tpu;
+  return t < s.total ? t : s.total;
+}
+// the CTA whose range holds tile t
+__host__ __device__ inline int64_t cta_of(const Sched& s, int64_t t) {
+  return (t + s.w * (t / s.tpu)) * s.grid / s.cost;
 }
 
 // Address of the 16-byte chunk holding V[tok][dim..dim+7] in a swizzled tile
@@ -366,8 +389,9 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
   float* lut = reinterpret_cast<float*>(smem + p.off_lut);
 
   const int64_t cta = blockIdx.x;
-  const int64_t t_begin = range_start(cta, p.total_tiles, p.grid);
-  const int64_t t_end = range_start(cta + 1, p.total_tiles, p.grid);
+  const Sched sched = make_sched(p.total_tiles, p.tpu, p.w_unit, p.grid);
+  const int64_t t_begin = range_start(sched, cta);
+  const int64_t t_end = range_start(sched, cta + 1);
 
   if (tid == 0) {
     for (int s = 0; s < p.stages; ++s) {
@@ -1041,8 +1065,10 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
     float* wo = lut;                                  // [8][R][D]
     float* wm = lut + CW * R * D;         // [8][R]
     float* wl = wm + CW * R;              // [8][R]
-    // merged unit rows for finalisation, after the per-warp scratch
+    // merged unit rows for finalisation, after the per-warp scratch, then the
+    // merge weights (per warp, or per cross-CTA partial, and row)
     float (*mo)[D] = reinterpret_cast<float (*)[D]>(lut + CW * R * (D + 2));
+    float* wt = lut + CW * R * (D + 2) + R * D;
     {
       const int n0 = 2 * (lane & 3);
       const int m0 = lane >> 2;
@@ -1064,25 +1090,35 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
     }
     if (ctid == 0) ms.is_last = 0;
     named_bar_sync(1, (CW * 32));
+    // one weight per (warp, row): e^(m_w - m*)
+    if (ctid < CW * R) {
+      const int w = ctid / R, r = ctid - w * R;
+      float mstar = -INFINITY;
+#pragma unroll
+      for (int x = 0; x < CW; ++x) mstar = fmaxf(mstar, wm[x * R + r]);
+      const float mg = wm[w * R + r];
+      wt[w * R + r] = (mg == -INFINITY) ? 0.f : fast_exp2((mg - mstar) * kLog2e);
+      if (w == 0) ms.mrow[r] = mstar;
+    }
+    named_bar_sync(1, (CW * 32));
     for (int e = ctid; e < R * D; e += (CW * 32)) {
       const int r = e / D, j = e - r * D;
-      float mstar = -INFINITY;
-      for (int w = 0; w < CW; ++w) mstar = fmaxf(mstar, wm[w * R + r]);
-      float O = 0.f, L = 0.f;
-      for (int w = 0; w < CW; ++w) {
-        const float mg = wm[w * R + r];
-        const float wt = (mg == -INFINITY) ? 0.f : exp2f((mg - mstar) * kLog2e);
-        O = fmaf(wo[(w * R + r) * D + j], wt, O);
-        L = fmaf(wl[w * R + r], wt, L);
-      }
+      float O = 0.f;
+#pragma unroll
+      for (int w = 0; w < CW; ++w) O = fmaf(wo[(w * R + r) * D + j], wt[w * R + r], O);
       mo[r][j] = O;
-      if (j == 0) { ms.mrow[r] = mstar; ms.lrow[r] = L; }
+    }
+    if (ctid < R) {
+      float L = 0.f;
+#pragma unroll
+      for (int w = 0; w < CW; ++w) L = fmaf(wl[w * R + ctid], wt[w * R + ctid], L);
+      ms.lrow[ctid] = L;
     }
     named_bar_sync(1, (CW * 32));
 
     // ---------------------------------------------- unit finalisation
-    const int64_t first = cta_of(u * p.tpu, p.total_tiles, p.grid);
-    const int64_t last = cta_of((u + 1) * p.tpu - 1, p.total_tiles, p.grid);
+    const int64_t first = cta_of(sched, u * p.tpu);
+    const int64_t last = cta_of(sched, (u + 1) * p.tpu - 1);
     const int ncov = static_cast<int>(last - first + 1);
     const int row_floats = D + 2;
     bool do_final = true;
@@ -1092,10 +1128,14 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
         const int r = e / row_floats, j = e - r * row_floats;
         slot[e] = j < D ? mo[r][j] : (j == D ? ms.mrow[r] : ms.lrow[r]);
       }
-      __threadfence();
       named_bar_sync(1, (CW * 32));
       if (ctid == 0) {
-        const int prev = atomicAdd(p.counters + u, 1);
+        // the barrier orders every thread's slot writes before this
+        // release; its acquire half makes the other partials visible to the
+        // CTA that arrives last
+        int prev;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                     : "=r"(prev) : "l"(p.counters + u) : "memory");
         if (prev == ncov - 1) {
           ms.is_last = 1;
           p.counters[u] = 0;  // leave the counter ready for the next launch
@@ -1106,21 +1146,34 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
       if (do_final) {
         __threadfence();
         const float* base = p.slots + (size_t)u * p.max_cov * R * row_floats;
+        // row maxima over the partials, then one weight per (partial, row)
+        if (ctid < R) {
+          float mstar = -INFINITY;
+#pragma unroll 4
+          for (int g = 0; g < ncov; ++g)
+            mstar = fmaxf(mstar, __ldcg(base + ((size_t)g * R + ctid) * row_floats + D));
+          ms.mrow[ctid] = mstar;
+        }
+        named_bar_sync(1, (CW * 32));
+        for (int e = ctid; e < ncov * R; e += (CW * 32)) {
+          const int r = e % R;
+          const float mg = __ldcg(base + (size_t)e * row_floats + D);
+          wt[e] = (mg == -INFINITY) ? 0.f : fast_exp2((mg - ms.mrow[r]) * kLog2e);
+        }
+        named_bar_sync(1, (CW * 32));
         for (int e = ctid; e < R * D; e += (CW * 32)) {
           const int r = e / D, j = e - r * D;
-          float mstar = -INFINITY;
+          float O = 0.f;
+#pragma unroll 4
           for (int g = 0; g < ncov; ++g)
-            mstar = fmaxf(mstar, __ldcg(base + ((size_t)g * R + r) * row_floats + D));
-          float O = 0.f, L = 0.f;
-          for (int g = 0; g < ncov; ++g) {
-            const float* row = base + ((size_t)g * R + r) * row_floats;
-            const float mg = __ldcg(row + D);
-            const float w = (mg == -INFINITY) ? 0.f : exp2f((mg - mstar) * kLog2e);
-            O = fmaf(__ldcg(row + j), w, O);
-            L = fmaf(__ldcg(row + D + 1), w, L);
-          }
+            O = fmaf(__ldcg(base + ((size_t)g * R + r) * row_floats + j), wt[g * R + r], O);
           mo[r][j] = O;
-          if (j == 0) { ms.mrow[r] = mstar; ms.lrow[r] = L; }
+        }
+        if (ctid < R) {
+          float L = 0.f;
+          for (int g = 0; g < ncov; ++g)
+            L = fmaf(__ldcg(base + ((size_t)g * R + ctid) * row_floats + D + 1), wt[g * R + ctid], L);
+          ms.lrow[ctid] = L;
         }
         named_bar_sync(1, (CW * 32));
       }
@@ -1191,7 +1244,7 @@ __global__ void lse_merge_kernel(const float* parts, int n_parts, int64_t rows, 
 
 // ------------------------------------------------------------------ host plan
 struct Plan {
-  int R, cw, tile, n_rg, n_ct, n_tt, tpu, grid, stages, max_cov, v_words, v_groups;
+  int R, cw, tile, n_rg, n_ct, n_tt, tpu, grid, stages, max_cov, v_words, v_groups, w_unit;
   int64_t total_tiles, n_units;
   uint32_t stage_bytes, off_idx, off_aux, off_vdq, off_lut, off_p, off_misc, off_vtab, v_tile_bytes;
   size_t smem;
@@ -1233,9 +1286,21 @@ int make_plan_r(const ss_decode_args* a, Plan& pl, int r_cap, int cw) {
   int64_t g = pl.total_tiles < sms ? pl.total_tiles : sms;
   if (a->max_ctas > 0 && g > a->max_ctas) g = a->max_ctas;
   pl.grid = static_cast<int>(g < 1 ? 1 : g);
-  const int64_t per_cta = pl.total_tiles / pl.grid;
-  pl.max_cov = static_cast<int>(pl.tpu / (per_cta > 0 ? per_cta : 1)) + 2;
-  if (pl.max_cov > pl.grid) pl.max_cov = pl.grid;
+  // a unit boundary inside a CTA's range (merge, cross-CTA publish, table
+  // reload) costs about as much as 14 tiles of streaming (measured, config 2)
+  pl.w_unit = pl.n_units > 1 ? 14 : 0;
+  {
+    // CTAs covering one unit: bounded by the shortest non-empty range (an
+    // empty range is a cost share inside a boundary's gap and covers no unit)
+    const Sched sc = make_sched(pl.total_tiles, pl.tpu, pl.w_unit, pl.grid);
+    int64_t shortest = pl.total_tiles;
+    for (int k = 0; k < pl.grid; ++k) {
+      const int64_t len = range_start(sc, k + 1) - range_start(sc, k);
+      if (len > 0 && len < shortest) shortest = len;
+    }
+    pl.max_cov = static_cast<int>(pl.tpu / (shortest > 0 ? shortest : 1)) + 2;
+    if (pl.max_cov > pl.grid) pl.max_cov = pl.grid;
+  }
   pl.v_words = 0;
   pl.v_groups = 0;
   int sbytes = 0;
@@ -1270,8 +1335,10 @@ int make_plan_r(const ss_decode_args* a, Plan& pl, int r_cap, int cw) {
   const size_t vtab = (a->vfmt == SS_V_VQ) ? (size_t)a->d * 256 * 2 : 0;
   // the LUT region doubles as the per-warp merge scratch at unit ends
   size_t lut = (size_t)nb * a->k * R * 4;
-  // per-warp merge scratch + the merged rows of the unit
-  const size_t scratch = (size_t)cw * R * (a->d + 2) * 4 + (size_t)R * a->d * 4;
+  // per-warp merge scratch + the merged rows of the unit + merge weights
+  // (per warp or per cross-CTA partial, and row)
+  const size_t n_wt = std::max<size_t>((size_t)cw, (size_t)pl.max_cov);
+  const size_t scratch = (size_t)cw * R * (a->d + 2) * 4 + (size_t)R * a->d * 4 + n_wt * R * 4;
   if (lut < scratch) lut = scratch;
   const size_t pbytes = (size_t)cw * slice_tokens(R) * 16;  // per-warp P slice [tokens][8] fp16
   fixed = vdq + vtab + ((lut + 127) & ~size_t(127)) + pbytes + ((sizeof(Misc) + 127) & ~size_t(127)) + 1024;
@@ -1452,6 +1519,7 @@ int run_decode(const ss_decode_args* a, float* part_out, void* stream) {
   p.tpu = pl.tpu; p.tc = a->tc; p.ttail = a->ttail; p.total_tiles = pl.total_tiles;
   p.n_units = pl.n_units; p.grid = pl.grid; p.stages = pl.stages;
   p.stage_shift = pl.stages == 4 ? 2 : (pl.stages == 2 ? 1 : 0); p.max_cov = pl.max_cov;
+  p.w_unit = pl.w_unit;
   p.q = a->q; p.qdt = a->q_dtype; p.q_sb = a->q_sb; p.q_sh = a->q_sh; p.q_st = a->q_st;
   p.scale = a->scale;
   p.perm = a->perm; p.rot_k = a->rot_k; p.cents = a->centroids; p.heavy = a->heavy;

@@ -111,3 +111,38 @@ def test_shard_range_covers_everything():
         spans = [splitkv.shard_range(n, r, w) for r in range(w)]
         assert spans[0][0] == 0 and spans[-1][1] == n
         assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+
+
+def test_decode_schedule_partition():
+    """The decode kernel's static schedule (csrc/decode_attn.cu: make_sched,
+    range_start, cta_of): ranges tile the (unit, tile) sequence in order,
+    every tile maps to the CTA whose range holds it, and no empty range sits
+    inside a unit (the cross-CTA merge counts every CTA of a unit)."""
+    import random
+    def make(total, tpu, w, grid): return (total, tpu, w, total + w * (total // tpu - 1), grid)
+    def start(s, k):
+        total, tpu, w, cost, grid = s
+        if k >= grid: return total
+        y = k * cost; pg = (tpu + w) * grid; j = y // pg; x = (y - j * pg + grid - 1) // grid
+        t = j * tpu + x if x < tpu else (j + 1) * tpu
+        return min(t, total)
+    def cta_of(s, t):
+        total, tpu, w, cost, grid = s
+        return (t + w * (t // tpu)) * grid // cost
+
+    rng = random.Random(1)
+    for _ in range(1500):
+        tpu = rng.choice([1, 2, 3, 7, 64, 65, 256, 4096])
+        nu = rng.randint(1, 200)
+        total = tpu * nu
+        grid = rng.randint(1, min(148, total))
+        w = 0 if nu == 1 else rng.choice([0, 1, 8, 20])
+        s = make(total, tpu, w, grid)
+        st = [start(s, k) for k in range(grid + 1)]
+        assert st[0] == 0 and st[-1] == total and all(a <= b for a, b in zip(st, st[1:]))
+        for t in range(0, total, max(1, total // 200)):
+            k = cta_of(s, t)
+            assert st[k] <= t < st[k + 1]
+        for u in range(nu):
+            f, l = cta_of(s, u * tpu), cta_of(s, (u + 1) * tpu - 1)
+            assert all(st[k + 1] > st[k] for k in range(f, l + 1))
