@@ -406,6 +406,104 @@ def _build_cfg4(device):
     return kcodec, caches, q
 
 
+def run_model(args, rank, local):
+    """Config 4 end to end: random-init Llama-style decoder (32 layers, 4096
+    hidden, 32q/8kv, FFN 14336, RoPE 1e6, bf16), per-layer block-VQ key and
+    value codecs (block_dim 4, 256 centroids) fit on the activations of a
+    dense 4096-token calibration pass, batch 32 x 4096-token random prompt,
+    then greedy decode steps with attention routed to sunshape_sdpa. Beside
+    it, the same decode with an uncompressed bf16 KV cache and torch's dense
+    SDPA (a library baseline)."""
+    import torch
+    from sunshape_mlx_b200 import harness as Hm, patch
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    cfg = Hm.DecoderConfig()
+    model = Hm.Decoder(cfg, device=device, seed=7)
+    g = torch.Generator(device=device).manual_seed(8)
+    calib = torch.randint(0, cfg.vocab, (1, 4096), generator=g, device=device)
+    t0 = time.perf_counter()
+    codecs = Hm.fit_layer_codecs(model, calib)
+    fit_s = time.perf_counter() - t0
+    B, T = 32, 4096
+    prompt = torch.randint(0, cfg.vocab, (B, T), generator=g, device=device)
+    steps = min(args.steps, 256)
+    warm = max(3, args.warmup)
+
+    def decode(caches, pos, ids, n):
+        for i in range(n):
+            logits = model.forward(ids, caches, pos + i)
+            ids = logits.argmax(-1, keepdim=True)
+        return ids
+
+    patch.apply()
+    caches = Hm.make_caches(model, codecs)
+    ids = model.forward(prompt, caches, 0).argmax(-1, keepdim=True)
+    ids = decode(caches, T, ids, warm)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(_gpu_id(local))
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    decode(caches, T + warm, ids, steps)
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1) / steps
+    kv_bytes = sum(c.nbytes for c in caches)
+    del caches
+    torch.cuda.empty_cache()
+
+    # the same decode over an uncompressed bf16 cache (torch SDPA)
+    class DenseCache:
+        def __init__(self, cap):
+            self.k = torch.empty((B, cfg.n_kv_heads, cap, cfg.head_dim), dtype=torch.bfloat16, device=device)
+            self.v = torch.empty_like(self.k)
+            self.n = 0
+
+        def append(self, k, v):
+            t = k.shape[2]
+            self.k[:, :, self.n:self.n + t] = k
+            self.v[:, :, self.n:self.n + t] = v
+            self.n += t
+
+    def dense_sdpa(q, k, v, cache, scale, mask, sinks=None):
+        return torch.nn.functional.scaled_dot_product_attention(
+            q, cache.k[:, :, :cache.n], cache.v[:, :, :cache.n], scale=scale, enable_gqa=True)
+
+    patch.revert()
+    dcaches = [DenseCache(T + warm + steps + 8) for _ in range(cfg.n_layers)]
+    orig = patch.current_sdpa
+    patch.current_sdpa = lambda: dense_sdpa
+    try:
+        ids = model.forward(prompt, dcaches, 0).argmax(-1, keepdim=True)
+        ids = decode(dcaches, T, ids, warm)
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        decode(dcaches, T + warm, ids, steps)
+        f1.record()
+        torch.cuda.synchronize()
+        dms = f0.elapsed_time(f1) / steps
+    finally:
+        patch.current_sdpa = orig
+    dense_bytes = 2 * cfg.n_layers * B * cfg.n_kv_heads * (T + warm + steps) * cfg.head_dim * 2
+    return {
+        "metric": "end-to-end decode tokens/s (config 4)", "value": B / (ms / 1e3), "unit": "tokens/s",
+        "n_gpus": 1, "steps": steps, "warmup": warm, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init weights N(0,0.02) seed 7, random prompt ids seed 8)",
+        "config": {"workload": "cfg4: Llama-style decoder 32 layers / 4096 hidden / 32q-8kv / FFN 14336, "
+                               "batch 32, 4096-token prompt, greedy decode; block-VQ K and V (bd 4, 256 "
+                               "centroids) per layer, attention via patch.apply() -> sunshape_sdpa",
+                   "global_batch": B, "seq_len": T, "parallelism": "single GPU"},
+        "kv_cache_bytes": kv_bytes, "dense_bf16_kv_cache_bytes": dense_bytes,
+        "dense_bf16_kv_ms_per_step": dms, "codec_fit_s": fit_s,
+        "gpu_launches": None, "clocks": clocks,
+    }
+
+
 def run_config(args, world, rank, local):
     import torch
     import torch.distributed as dist
@@ -752,6 +850,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--config", type=int, choices=[2, 3, 4, 5], default=2,
                     help="decode configuration (BASELINE configs 2, 3, 5; 4 = config-4 attention)")
+    ap.add_argument("--model", action="store_true",
+                    help="with --config 4: the end-to-end decoder (tokens/s) instead of attention alone")
     ap.add_argument("--assign", action="store_true",
                     help="benchmark the cache-fill quantize (ss_vq_assign) instead of decode")
     ap.add_argument("--assign-path", choices=["tensor", "simt", "auto"], default="tensor")
@@ -782,6 +882,11 @@ def main():
     if world > 1:
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    if args.config == 4 and args.model:
+        line = run_model(args, rank, local)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
     if args.config != 2:
         try:
             line = run_config(args, world, rank, local)
