@@ -17,7 +17,7 @@ import torch
 
 from . import _lib as L
 from . import kernels as K
-from .cache import SunShapeKVCache
+from .cache import HybridSunShapeKVCache, SunShapeKVCache
 
 __all__ = ["sunshape_sdpa", "decode_partials", "workspace_for", "PreparedDecode"]
 
@@ -185,7 +185,8 @@ def sunshape_sdpa(queries, cache, scale: float, mask=None) -> torch.Tensor:
     tkv = cache.offset
     if tkv == 0:
         return torch.zeros_like(q)
-    if mask is None and isinstance(cache, SunShapeKVCache):
+    if mask is None and (isinstance(cache, SunShapeKVCache) or
+                         (isinstance(cache, HybridSunShapeKVCache) and cache._buffer_offset == 0)):
         return _sdpa_simple_fast(q, cache, scale)
     codec = cache.codec
     spec = cache.attention_spec()
@@ -202,13 +203,16 @@ def sunshape_sdpa(queries, cache, scale: float, mask=None) -> torch.Tensor:
 
 
 def _sdpa_simple_fast(q: torch.Tensor, cache, scale: float) -> torch.Tensor:
-    """sunshape_sdpa for the simple cache without a mask: the argument block
+    """sunshape_sdpa without a mask for the simple cache, or a hybrid cache
+    whose fp16 tail is empty (then every token is compressed): the argument block
     is kept on the cache and rebuilt only when the storage is reallocated or
     the query layout, dtype or scale changes; per call only the query and
     output pointers and the token count are updated."""
     codec = cache.codec
+    vcod = getattr(cache, "value_codec", None)
     key = (cache._epoch, tuple(q.shape), tuple(q.stride()), q.dtype, float(scale),
-           codec.centroids.data_ptr(), codec.permutation.data_ptr(), codec.use_rotation)
+           codec.centroids.data_ptr(), codec.permutation.data_ptr(), codec.use_rotation,
+           None if vcod is None else (vcod.centroids.data_ptr(), vcod.centroids._version))
     memo = cache._sdpa_memo
     if memo is None or memo[0] != key:
         spec = cache.attention_spec()

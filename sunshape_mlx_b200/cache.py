@@ -351,6 +351,9 @@ class HybridSunShapeKVCache:
         self._value_indices = None
         self._values_fp16 = None
         self._compressed_capacity = 0
+        self._epoch = 0          # bumped whenever compressed storage is reallocated
+        self._assign_memo = None
+        self._sdpa_memo = None
 
     @property
     def offset(self) -> int:
@@ -362,6 +365,7 @@ class HybridSunShapeKVCache:
         if need <= self._compressed_capacity:
             return
         cap = _round_up(need, _STEP)
+        self._epoch += 1
         H, dev, u = self.n_kv_heads, self.device, self._compressed_offset
         self._key_indices = _grow(self._key_indices, (B, H, cap, self.n_blocks), u, torch.uint8, dev)
         nh = self.codec.n_heavy_blocks
@@ -432,6 +436,8 @@ class HybridSunShapeKVCache:
         if self._batch and B != self._batch:
             raise ValueError(f"batch size changed from {self._batch} to {B}")
         self._batch = B
+        if self.buffer_size == 0 and self._buffer_offset == 0 and self._append_vq_fast(k, v):
+            return
         need = self._buffer_offset + T
         cur = 0 if self._key_buffer is None else self._key_buffer.shape[2]
         if need > cur:
@@ -556,6 +562,53 @@ class HybridSunShapeKVCache:
     @property
     def can_fuse_value_dequant(self) -> bool:
         return self.value_backend == "grouped" and self._compressed_offset > 0
+
+    def _append_vq_fast(self, k: torch.Tensor, v: torch.Tensor) -> bool:
+        """No fp16 tail and block-VQ values: new keys and values go straight
+        into the index streams, one ss_vq_assign each, from argument tuples
+        kept until the storage is reallocated (a decode step's append is
+        otherwise dominated by host work). Same indices as the buffered path,
+        which quantizes the same fp16-stored tokens."""
+        kc, vc = self.codec, self.value_codec
+        if (self.value_backend != "sunshape" or kc.use_rotation or vc.use_rotation
+                or kc.n_heavy_blocks or vc.n_heavy_blocks):
+            return False
+        B, H, T, D = k.shape
+        # the buffered path stores tokens in fp16 before quantizing them
+        k16 = k if k.dtype == torch.float16 else k.half()
+        v16 = v if v.dtype == torch.float16 else v.half()
+        for t in (k16, v16):
+            if t.stride(3) != 1 or t.stride(0) != H * t.stride(1):
+                return False
+        self._ensure_compressed(B, T)
+        key = (self._epoch, k16.stride(1), k16.stride(2), v16.stride(1), v16.stride(2),
+               kc.centroids.data_ptr(), vc.centroids.data_ptr(), kc.permutation.data_ptr(),
+               vc.permutation.data_ptr())
+        memo = self._assign_memo
+        if memo is None or memo[0] != key:
+            L = K.L
+            fn = L.load().ss_vq_assign
+            calls = []
+            for cd, src, dst in ((kc, k16, self._key_indices), (vc, v16, self._value_indices)):
+                perm = cd.permutation if cd._is_perm() else None
+                calls.append((src is k16, L.ptr(perm), L.ptr(cd.centroids), cd.block_dim,
+                              cd.n_centroids, dst.data_ptr(), dst.stride(1), dst.stride(2),
+                              src.stride(1), src.stride(2), [perm, cd]))
+            memo = (key, fn, calls)
+            self._assign_memo = memo
+        _, fn, calls = memo
+        o = self._compressed_offset
+        st = K.L.stream_ptr(self.device)
+        C = K.L.C
+        for is_key, perm_p, cents_p, bd, kn, dst_p, dgs, drs, sgs, srs, _ in calls:
+            src = k16 if is_key else v16
+            rc = fn(C.c_void_p(src.data_ptr()), K.L.SS_F16, B * H, T, sgs, srs, D, perm_p, cents_p,
+                    bd, kn, None, C.c_void_p(dst_p + o * drs), dgs, drs, None, 0, 0, None, 0, st)
+            if rc:
+                K.L.check("ss_vq_assign", rc)
+        self._compressed_offset += T
+        self.last_value_quant_backend = "sunshape"
+        return True
 
     def _vq_transformed(self) -> bool:
         vc = self.value_codec
