@@ -218,7 +218,7 @@ __device__ __forceinline__ void unit_codec_rows(const DecodeParams& p, const flo
 // sub-vectors in registers) and centroids t % 64 + i * 64, so a warp writes
 // contiguous table rows.
 // BD = 0 is the generic path for block sizes other than 4 and 8.
-constexpr int kLutBlocks = 4;
+constexpr int kLutBlocks = 8;
 template <int R, int BD>
 __global__ void __launch_bounds__(kLutThreads) lut_kernel(const __grid_constant__ DecodeParams p) {
   // only this unit's R query rows (keeps the CTA small enough to share an SM
@@ -241,9 +241,10 @@ __global__ void __launch_bounds__(kLutThreads) lut_kernel(const __grid_constant_
       const int b = b0 + tid / TPB, cl = tid % TPB;
       const bool bok = b < p.nb;
       const float* cb = p.cents + (size_t)(bok ? b : 0) * p.k * BD;
-      float cv[4][BD];
+      constexpr int NCV = (256 + TPB - 1) / TPB;  // centroid rows per thread (k <= 256)
+      float cv[NCV][BD];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < NCV; ++i) {
         const int c = cl + i * TPB;
 #pragma unroll
         for (int j = 0; j < BD; j += 4) {
@@ -290,7 +291,7 @@ __global__ void __launch_bounds__(kLutThreads) lut_kernel(const __grid_constant_
         for (int j = 0; j < BD; ++j) q[r][j] = zero ? 0.f : qo[r][pj[j]];
       float* ob = out + (size_t)b * p.k * R;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < NCV; ++i) {
         const int c = cl + i * TPB;
         if (c >= p.k) break;
         float o[R];
