@@ -136,6 +136,11 @@ int ss_kmeans_update(const float* data, int64_t n, int nb, int bd, const uint8_t
 int ss_vq_scores(const float* q, int nq, int d, const float* centroids, int bd, int k,
                  const uint8_t* idx, int64_t t, int64_t idx_row_stride, float* out,
                  int64_t out_stride, void* stream);
+/* Query x centroid table (SunShapeBlockCodec.precompute_query_centroid_dots,
+ * codec.py:553-573): out f32 (nq, nb, k), out[q][b][c] = sum_j q[q][b*bd + j]
+ * * centroids[b][c][j], q f32 (nq, d) contiguous, already in codec space. */
+int ss_query_centroid_dots(const float* q, int64_t nq, int d, const float* centroids, int bd,
+                           int k, float* out, void* stream);
 /* Same gather from a precomputed table qdots f32 (nq, nb, k)
  * (block_vq_score_metal's input, kernels.py:87-116). */
 int ss_vq_scores_lut(const float* qdots, int nq, int nb, int k, const uint8_t* idx, int64_t t,
@@ -279,6 +284,15 @@ typedef struct ss_decode_args {
    * share a workspace must be stream-ordered. */
   void* workspace; size_t workspace_bytes;
   int max_ctas;              /* 0 = all SMs */
+  /* Bound of every device-side wait of this launch in nanoseconds (<= 0:
+   * 2 s). A wait that runs out makes the launch give up: the output is then
+   * invalid, the workspace's error word and the process error sink (see
+   * ss_set_error_sink) report SS_ERR_TIMEOUT. */
+  int64_t wait_limit_ns;
+  /* Test hook, 0 in normal use: t > 0 makes the producer skip the copies of
+   * flattened tile t - 1 while still expecting their bytes, so the waits on
+   * that tile run out (exercises the timeout path without a GPU fault). */
+  int64_t test_skip_tile;
 } ss_decode_args;
 
 size_t ss_decode_workspace_size(const ss_decode_args* a);
@@ -300,6 +314,26 @@ int ss_decode_attn_noalloc(const ss_decode_args* a, void* stream);
 /* Reads and clears the sticky device-side error word of a decode workspace
  * (synchronizes the stream). Returns SS_OK or SS_ERR_TIMEOUT. */
 int ss_decode_check(void* workspace, void* stream);
+
+/* ss_decode_check for the fixed scratch array of ss_decode_attn_noalloc on the
+ * current device (whose address its callers never see). */
+int ss_decode_noalloc_check(void* stream);
+
+/* Process-wide error sink (no counterpart in the reference, whose wrappers
+ * return None and fall back): host_word is a page-locked host int (from
+ * cudaHostAlloc / cudaMallocHost, visible to the device under unified
+ * addressing). Every later launch of the decode and the tensor-core
+ * assignment kernels ORs a nonzero code into it when one of its bounded
+ * waits gives up (1/2/4/8: decode producer/drain/tile/table waits; 16: the
+ * assignment pipeline), with a system-scope atomic, so the host can detect a
+ * failed launch by reading the word, without synchronizing. NULL detaches
+ * the sink. The caller reads and clears the word. */
+int ss_set_error_sink(int* host_word);
+
+/* Bound of the tensor-core assignment kernel's pipeline waits (<= 0: 2 s)
+ * and a test hook (skip_tile > 0: the loader never stages tile
+ * skip_tile - 1, so the waits on it run out). Process-wide; for tests. */
+int ss_set_assign_wait(int64_t wait_limit_ns, int64_t skip_tile);
 
 /* Split-KV partials merge across shards (multi-GPU long context): parts is
  * f32 [n_parts][rows][d + 2] holding (o unnormalized[d], m, l) per row;

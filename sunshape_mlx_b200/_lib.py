@@ -18,6 +18,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libsunshape_b200.so")
 
 SS_OK = 0
+SS_ERR_TIMEOUT = 4
 STATUS_NAMES = {1: "bad argument", 2: "unsupported", 3: "CUDA error", 4: "timeout",
                 5: "workspace"}
 SS_F32, SS_F16, SS_BF16 = 0, 1, 2
@@ -70,6 +71,7 @@ class DecodeArgs(C.Structure):
         ("out", vp), ("out_dtype", i32), ("o_sb", i64), ("o_sh", i64), ("o_st", i64),
         ("workspace", vp), ("workspace_bytes", C.c_size_t),
         ("max_ctas", i32),
+        ("wait_limit_ns", i64), ("test_skip_tile", i64),
     ]
 
 
@@ -120,6 +122,10 @@ _SIGS = {
     "ss_vq_assign_check": ([vp], i32),
     "ss_decode_attn_noalloc": ([C.POINTER(DecodeArgs), vp], i32),
     "ss_lse_merge": ([vp, i32, i64, i32, vp, vp, i32, i64, vp], i32),
+    "ss_decode_noalloc_check": ([vp], i32),
+    "ss_set_error_sink": ([vp], i32),
+    "ss_set_assign_wait": ([i64, i64], i32),
+    "ss_query_centroid_dots": ([vp, i64, i32, vp, i32, i32, vp, vp], i32),
 }
 
 EXPORTED = tuple(_SIGS)
@@ -145,7 +151,53 @@ def load(path: str | None = None) -> C.CDLL:
             fn.argtypes = argt
             fn.restype = rest
         _lib = lib
+        _attach_error_sink(lib)
         return lib
+
+
+# ------------------------------------------------------------------ device-side give-ups
+# A page-locked host word that the decode and tensor-core assignment kernels
+# OR a code into when one of their bounded waits gives up (ss_set_error_sink).
+# Reading it costs no synchronization, so every product entry point checks it
+# before launching and raises for a launch that failed earlier.
+_SINK = None
+_SINK_WORD = None
+
+
+def _attach_error_sink(lib) -> None:
+    global _SINK, _SINK_WORD
+    if not torch.cuda.is_available():
+        return
+    t = torch.zeros(1, dtype=torch.int32).pin_memory()
+    if lib.ss_set_error_sink(C.c_void_p(t.data_ptr())) != SS_OK:
+        raise SunShapeCudaError("ss_set_error_sink", 1, lib.ss_last_error().decode())
+    _SINK = t
+    _SINK_WORD = C.c_int.from_address(t.data_ptr())
+
+
+WAIT_CODES = {1: "decode producer stage wait", 2: "decode copy drain", 4: "decode tile wait",
+              8: "decode table wait", 16: "tensor-core assignment pipeline wait"}
+
+
+def poll_device_errors() -> None:
+    """Raises SunShapeCudaError (SS_ERR_TIMEOUT) if a kernel launched since
+    the last poll gave up on a bounded device-side wait; its output was then
+    invalid. Clears the word. Does not synchronize: a launch still running is
+    seen by a later poll (``check_device_errors`` synchronizes first)."""
+    w = _SINK_WORD
+    if w is None or w.value == 0:
+        return
+    code = w.value
+    w.value = 0
+    what = ", ".join(n for b, n in WAIT_CODES.items() if code & b) or str(code)
+    raise SunShapeCudaError("device wait", SS_ERR_TIMEOUT,
+                            f"a device-side wait gave up ({what}); the output of that launch is invalid")
+
+
+def check_device_errors(device=None) -> None:
+    """Synchronizes the current stream of `device`, then ``poll_device_errors``."""
+    torch.cuda.current_stream(device).synchronize()
+    poll_device_errors()
 
 
 def last_error() -> str:

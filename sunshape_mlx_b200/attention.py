@@ -171,13 +171,25 @@ def _prepare_mask(mask, tq: int, tkv: int, device) -> tuple[torch.Tensor | None,
     return m.to(torch.float32).contiguous(), 0, False
 
 
-def sunshape_sdpa(queries, cache, scale: float, mask=None) -> torch.Tensor:
+def sunshape_sdpa(queries, cache, scale: float, mask=None, *, check: bool = False) -> torch.Tensor:
     """Scaled dot-product attention over a SunShape cache (attention.py:166-352).
 
     queries (B, n_q_heads, T_q, D) in the model basis; the cache's key indices,
     value payload and (hybrid) fp16 tail are read in place. Output has the
     queries' dtype.
+
+    Every call first raises SunShapeCudaError (timeout) if an earlier launch
+    gave up on a bounded device-side wait (its output was invalid); with
+    ``check=True`` the call also synchronizes and checks its own launch.
     """
+    L.poll_device_errors()
+    out = _sdpa(queries, cache, scale, mask)
+    if check:
+        L.check_device_errors(out.device)
+    return out
+
+
+def _sdpa(queries, cache, scale: float, mask=None) -> torch.Tensor:
     q = K.cuda_tensor(queries, device=cache.device)
     B, Hq, Tq, D = q.shape
     if Hq % cache.n_kv_heads:
@@ -256,6 +268,7 @@ def _sdpa_simple_fast(q: torch.Tensor, cache, scale: float) -> torch.Tensor:
 def decode_partials(queries, cache, scale: float) -> torch.Tensor:
     """This shard's unnormalised (o, m, l) per query row, f32
     (B * Hq * Tq, D + 2): the input of the cross-GPU log-sum-exp merge."""
+    L.poll_device_errors()
     q = K.cuda_tensor(queries, device=cache.device)
     B, Hq, Tq, D = q.shape
     part = torch.empty((B * Hq * Tq, D + 2), dtype=torch.float32, device=q.device)
@@ -282,7 +295,7 @@ class PreparedDecode:
     ``out`` in place."""
 
     def __init__(self, q: torch.Tensor, cache, scale: float, out: torch.Tensor | None = None,
-                 max_ctas: int = 0):
+                 max_ctas: int = 0, wait_limit_ns: int = 0, _test_skip_tile: int = -1):
         codec = cache.codec
         self.q = q
         self.out = out if out is not None else torch.empty_like(q)
@@ -301,13 +314,27 @@ class PreparedDecode:
         self.ws = workspace_for(q.device, nbytes)
         self._a.workspace = self.ws.data_ptr()
         self._a.workspace_bytes = self.ws.numel()
+        # bound of the kernel's device-side waits (0: 2 s); the skip hook makes
+        # the waits on one tile run out (tests of the timeout path)
+        self._a.wait_limit_ns = int(wait_limit_ns)
+        self._a.test_skip_tile = int(_test_skip_tile) + 1 if _test_skip_tile >= 0 else 0
         self._lib = lib
         self._ref = C.byref(self._a)
         self.device = q.device
 
-    def run(self, stream=None) -> torch.Tensor:
+    def run(self, stream=None, check: bool = False) -> torch.Tensor:
+        """One launch. Raises first if an earlier launch gave up on a bounded
+        device-side wait; ``check=True`` also synchronizes the stream and
+        checks this launch."""
+        w = L._SINK_WORD
+        if w is not None and w.value:
+            L.poll_device_errors()
         st = C.c_void_p(stream if stream is not None else torch.cuda.current_stream(self.device).cuda_stream)
         rc = self._lib.ss_decode_attn(self._ref, st)
         if rc:
             L.check("ss_decode_attn", rc)
+        if check:
+            if stream is not None:
+                torch.cuda.synchronize(self.device)
+            L.check_device_errors(self.device)
         return self.out

@@ -17,12 +17,13 @@ from __future__ import annotations
 
 import torch
 
+from . import _lib as L
 from . import kernels as K
 from .codec import SunShapeBlockCodec
 from .value_codecs import GroupedValueCodec, TurboQuantValueCodec, build_value_codec
 
 __all__ = ["SunShapeKVCache", "HybridSunShapeKVCache", "create_kv_cache", "save_cache",
-           "load_cache"]
+           "load_cache", "DeferredTensor"]
 
 _STEP = 256
 _DEFAULT_BUFFER_SIZE = 128
@@ -54,6 +55,90 @@ def _causal_mask(offset: int, n: int, return_array: bool):
         torch.float16)
 
 
+class DeferredTensor:
+    """A tensor computed on first use: what ``update_and_fetch`` returns for
+    the dequantized keys (and decoded values), which mlx-lm-style callers
+    pass straight to the patched SDPA. The fused kernel reads the cache's
+    streams in place and never looks at them, so materializing them on every
+    step (a full O(T) dequantization per layer, cache.py:205, 211-240 of the
+    reference) is skipped unless something actually reads them.
+
+    ``shape``/``dtype``/``device``/``ndim`` are known without computing; any
+    other use (indexing, arithmetic, torch functions, attribute access)
+    materializes it once, from the cache's storage at that moment with the
+    token count of the call that made it. A caller that keeps it across a
+    later append, flush or trim calls ``materialize()`` first."""
+
+    __slots__ = ("_fn", "_shape", "_dtype", "_device", "_t")
+
+    def __init__(self, fn, shape, dtype, device):
+        self._fn, self._shape, self._dtype, self._device, self._t = fn, torch.Size(shape), dtype, device, None
+
+    shape = property(lambda self: self._shape)
+    dtype = property(lambda self: self._dtype)
+    device = property(lambda self: self._device)
+    ndim = property(lambda self: len(self._shape))
+    is_materialized = property(lambda self: self._t is not None)
+
+    def size(self, dim=None):
+        return self._shape if dim is None else self._shape[dim]
+
+    def dim(self) -> int:
+        return len(self._shape)
+
+    def materialize(self) -> torch.Tensor:
+        if self._t is None:
+            self._t = self._fn()
+            self._fn = None
+        return self._t
+
+    def __getattr__(self, name):
+        return getattr(self.materialize(), name)
+
+    @classmethod
+    def __torch_function__(cls, func, types, args=(), kwargs=None):
+        def conv(x):
+            if isinstance(x, DeferredTensor):
+                return x.materialize()
+            if isinstance(x, (list, tuple)):
+                return type(x)(conv(y) for y in x)
+            if isinstance(x, dict):
+                return {k: conv(v) for k, v in x.items()}
+            return x
+        return func(*conv(args), **conv(kwargs or {}))
+
+    def __getitem__(self, i):
+        return self.materialize()[i]
+
+    def __len__(self) -> int:
+        return self._shape[0]
+
+    def __iter__(self):
+        return iter(self.materialize())
+
+    def __array__(self, dtype=None):
+        a = self.materialize().cpu().numpy()
+        return a if dtype is None else a.astype(dtype)
+
+    def __repr__(self) -> str:
+        state = "materialized" if self._t is not None else "deferred"
+        return f"DeferredTensor(shape={tuple(self._shape)}, dtype={self._dtype}, {state})"
+
+
+def _binop(name):
+    def f(self, *a):
+        return getattr(self.materialize(), name)(*[x.materialize() if isinstance(x, DeferredTensor) else x for x in a])
+    f.__name__ = name
+    return f
+
+
+for _n in ("__add__", "__radd__", "__sub__", "__rsub__", "__mul__", "__rmul__", "__truediv__",
+           "__rtruediv__", "__matmul__", "__rmatmul__", "__neg__", "__pow__", "__eq__", "__ne__",
+           "__lt__", "__le__", "__gt__", "__ge__", "__abs__"):
+    setattr(DeferredTensor, _n, _binop(_n))
+DeferredTensor.__hash__ = object.__hash__
+
+
 class SunShapeKVCache:
     """Keys as block-VQ indices + fp16 values (cache.py:59-336)."""
 
@@ -76,6 +161,7 @@ class SunShapeKVCache:
         self._epoch = 0          # bumped whenever the storage is reallocated
         self._assign_memo = None
         self._sdpa_memo = None
+        self.eager_fetch = False  # True: update_and_fetch materializes keys (reference behaviour)
 
     # ------------------------------------------------------------ storage
     def _ensure_capacity(self, B: int, new_tokens: int) -> None:
@@ -102,6 +188,7 @@ class SunShapeKVCache:
     def append(self, keys, values) -> None:
         """Quantize and store new tokens without materialising anything
         (the write half of update_and_fetch)."""
+        L.poll_device_errors()
         k = K.cuda_tensor(keys, device=self.device)
         v = K.cuda_tensor(values, device=self.device)
         B, H, T, D = k.shape
@@ -168,10 +255,21 @@ class SunShapeKVCache:
         return True
 
     def update_and_fetch(self, keys, values):
-        """cache.py:156-205: append, then return (keys, values) as stored
-        (keys dequantized); the fused SDPA does not use the returned keys."""
+        """cache.py:156-205: append, then return (keys, values) as stored.
+        The keys are a DeferredTensor (dequantized on first use only: the
+        fused SDPA reads the index stream itself); ``eager_fetch = True``
+        returns the dequantized tensor at once, as the reference does."""
         self.append(keys, values)
-        return self.keys, self.values
+        return self._fetch_keys(), self.values
+
+    def _fetch_keys(self):
+        if self.eager_fetch or self._key_indices is None or self.offset == 0:
+            return self.keys
+        idx, kh, t = self._key_indices, self._key_heavy, self.offset
+        codec = self.codec
+        return DeferredTensor(
+            lambda: _dequantize_keys(codec, idx[:, :, :t], None if kh is None else kh[:, :, :t]),
+            (self._batch, self.n_kv_heads, t, self.head_dim), torch.float32, self.device)
 
     # ------------------------------------------------------------ views
     @property
@@ -354,6 +452,7 @@ class HybridSunShapeKVCache:
         self._epoch = 0          # bumped whenever compressed storage is reallocated
         self._assign_memo = None
         self._sdpa_memo = None
+        self.eager_fetch = False  # True: update_and_fetch materializes (reference behaviour)
 
     @property
     def offset(self) -> int:
@@ -428,6 +527,7 @@ class HybridSunShapeKVCache:
 
     def append(self, keys, values) -> None:
         """Append to the fp16 buffer and flush overflow (cache.py:656-710)."""
+        L.poll_device_errors()
         k = K.cuda_tensor(keys, device=self.device)
         v = K.cuda_tensor(values, device=self.device)
         B, H, T, D = k.shape
@@ -465,8 +565,23 @@ class HybridSunShapeKVCache:
             self._flush_buffer(B, self._buffer_offset - self.buffer_size)
 
     def update_and_fetch(self, keys, values):
+        """cache.py:656-710. Keys and values come back as DeferredTensors
+        (computed on first use; the fused SDPA reads the streams itself);
+        ``eager_fetch = True`` materializes them at once, as the reference."""
         self.append(keys, values)
-        return self.keys, self.values
+        if self.eager_fetch or self.offset == 0:
+            return self.keys, self.values
+        shape = (max(self._batch, 1), self.n_kv_heads, self.offset, self.head_dim)
+        snap = self._snapshot()
+        return (DeferredTensor(lambda: snap.keys, shape, torch.float32, self.device),
+                DeferredTensor(lambda: snap.values, shape, self.dtype, self.device))
+
+    def _snapshot(self):
+        """A shallow copy holding the current streams and offsets (the token
+        counts of this call for views computed later)."""
+        import copy
+
+        return copy.copy(self)
 
     # ------------------------------------------------------------ views
     @property

@@ -321,10 +321,15 @@ class SunShapeBlockCodec:
 
     # ------------------------------------------------------------ scores
     def precompute_query_centroid_dots(self, query) -> torch.Tensor:
-        """qdots[q, b, c] = <q_b, C[b, c]> (codec.py:553-573); query in codec space."""
-        q = K.cuda_tensor(query, torch.float32, self.device)
-        qb = q.reshape(q.shape[0], self.n_blocks, self.block_dim)
-        return torch.einsum("qbd,bcd->qbc", qb, self.centroids)
+        """qdots[q, b, c] = <q_b, C[b, c]> (codec.py:553-573); query (n_qh,
+        head_dim) already in codec space. One launch of ss_query_centroid_dots."""
+        q = K.cuda_tensor(query, torch.float32, self.device).reshape(-1, self.head_dim).contiguous()
+        out = torch.empty((q.shape[0], self.n_blocks, self.n_centroids), dtype=torch.float32,
+                          device=self.device)
+        K.L.call("ss_query_centroid_dots", K.L.ptr(q), q.shape[0], self.head_dim,
+                 K.L.ptr(self.centroids), self.block_dim, self.n_centroids, K.L.ptr(out),
+                 K.L.stream_ptr(self.device))
+        return out
 
     def attention_scores(self, query, quantized: SunShapeQuantized, *,
                          prefer_metal: bool = True) -> torch.Tensor:

@@ -47,6 +47,8 @@
 //               padded shared-memory tile) as far ahead as the ring allows
 // A sequence step is one (tile, block) pair; blocks of a CTA are a contiguous
 // group of the codec's blocks whose B operands stay resident in shared memory.
+#include <atomic>
+
 #include "common.cuh"
 #include "vq_math.cuh"
 
@@ -84,6 +86,9 @@ struct TcParams {
   int slots;              // A ring depth
   int nstage;             // staged key tiles in flight (2 or 3)
   int64_t tpg, n_tiles;   // 128-row tiles per group, total tiles
+  uint64_t wait_ns;       // bound of every pipeline wait
+  int64_t skip_tile;      // test hook: tile the loader never stages (-1: none)
+  int* sink;              // process error sink (host word) or null
   // dynamic shared-memory offsets (bytes, from the 1024-aligned base)
   uint32_t off_b, off_a, off_stage, off_cf, off_misc, stage_bytes, stage_stride;
 };
@@ -189,13 +194,15 @@ struct Bar {
   uint64_t* t_empty;  // [2] epilogue group -> MMA (4 arrivals)
 };
 
-__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                        const TcParams& p) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (global_ns() - t0 > kTcWaitNs) {
+    if (global_ns() - t0 > p.wait_ns) {
+      if (!*abort) report_wait_failure(nullptr, p.sink, 16);
       *abort = 1;
       atomicOr(&g_assign_status, 1u);
       return false;
@@ -402,13 +409,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // After an abandoned wait the loops keep running without work.
     for (int64_t tile = tfirst; tile < p.n_tiles; tile += tstride, ++li) {
       const int sb = li % p.nstage;
-      if (ok) ok = tc_wait(st_full + sb, (li / p.nstage) & 1, s_abort);
+      if (ok) ok = tc_wait(st_full + sb, (li / p.nstage) & 1, s_abort, p);
       const uint8_t* st = s_stage + (size_t)sb * p.stage_bytes;
       for (int bl = 0; bl < nbl; ++bl, ++n) {
         const int b = b0 + bl;
         const uint32_t slot = n % p.slots;
-        if (ok) ok = tc_wait(a_empty + slot, ((n / p.slots) & 1) ^ 1, s_abort);
-        if (ok) ok = tc_wait(kn_empty + n % kKnRing, ((n / kKnRing) & 1) ^ 1, s_abort);
+        if (ok) ok = tc_wait(a_empty + slot, ((n / p.slots) & 1) ^ 1, s_abort, p);
+        if (ok) ok = tc_wait(kn_empty + n % kKnRing, ((n / kKnRing) & 1) ^ 1, s_abort, p);
         if (!ok) continue;
         uint8_t* dst = s_a + (size_t)slot * a_slot_bytes;
         float* kn_out = s_kn + (n % kKnRing) * kTcRows;
@@ -490,7 +497,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     for (int64_t tile = tfirst; tile < p.n_tiles; tile += tstride, ++li) {
       const int buf = li % p.nstage;
       const uint32_t use = li / p.nstage;
-      if (use > 0 && !__all_sync(0xffffffffu, tc_wait(st_empty + buf, (use - 1) & 1, s_abort))) break;
+      if (use > 0 && !__all_sync(0xffffffffu, tc_wait(st_empty + buf, (use - 1) & 1, s_abort, p))) break;
+      if (tile == p.skip_tile) continue;  // test hook: this stage never fills
       const int64_t g = tile / p.tpg;
       const int64_t t0 = (tile - g * p.tpg) * kTcRows;
       const uint8_t* src0 =
@@ -504,6 +512,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       cp_async_mbar_arrive(st_full + buf);
     }
+    // copies of this lane still in flight after a give-up land before exit
+    asm volatile("cp.async.wait_all;" ::: "memory");
   } else if (warp == kTcMmaWarp) {
     // TMEM owner: allocated above, released below; the epilogue groups
     // issue their own MMAs.
@@ -525,8 +535,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     auto issue_mma = [&](uint32_t q) -> bool {
       const uint32_t slot = q % p.slots;
       const int qbl = (int)(q % nbl);
-      if (!tc_wait(t_empty + eg, ((q >> 1) & 1) ^ 1, s_abort)) return false;
-      if (!tc_wait(a_full + slot, (q / p.slots) & 1, s_abort)) return false;
+      if (!tc_wait(t_empty + eg, ((q >> 1) & 1) ^ 1, s_abort, p)) return false;
+      if (!tc_wait(a_full + slot, (q / p.slots) & 1, s_abort, p)) return false;
       tc_fence_after();
       const uint32_t a_addr = a0 + slot * a_slot_bytes;
       const uint32_t b_addr = bb0 + qbl * b_blk_bytes;
@@ -555,14 +565,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const bool valid = t < p.rpg;
       {
         const int b = b0 + bl;
-        ok = __all_sync(0xffffffffu, tc_wait(t_full + eg, (n >> 1) & 1, s_abort));
+        ok = __all_sync(0xffffffffu, tc_wait(t_full + eg, (n >> 1) & 1, s_abort, p));
         if (!ok) break;
         tc_fence_after();
         const bool heavy = s_heavy[b] != 0;
         int idx = 0;
         bool need = false;
         // the producers' scaled squared key norm of this row (NaN: exact path)
-        ok = __all_sync(0xffffffffu, tc_wait(kn_full + n % kKnRing, (n / kKnRing) & 1, s_abort));
+        ok = __all_sync(0xffffffffu, tc_wait(kn_full + n % kKnRing, (n / kKnRing) & 1, s_abort, p));
         if (!ok) break;
         const float kn = s_kn[(n % kKnRing) * kTcRows + row];
         __syncwarp();
@@ -685,6 +695,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 }  // namespace
 
 // ---------------------------------------------------------------- host side
+std::atomic<int64_t> g_tc_wait_ns{0};     // ss_set_assign_wait (tests)
+std::atomic<int64_t> g_tc_skip_tile{0};
+
 // Returns SS_ERR_UNSUPPORTED when the tensor-core path does not apply.
 int launch_vq_assign_tc(const void* keys, int key_dtype, int64_t n_groups, int64_t rpg,
                         int64_t kgs, int64_t krs, int d, const int32_t* perm,
@@ -734,6 +747,9 @@ int launch_vq_assign_tc(const void* keys, int key_dtype, int64_t n_groups, int64
   p.out_pt = out_pt; p.dist_mode = dist_mode;
   p.n_grp = n_grp; p.gsize = gsize; p.slots = slots; p.nstage = nstage;
   p.tpg = (rpg + kTcRows - 1) / kTcRows;
+  p.wait_ns = g_tc_wait_ns > 0 ? static_cast<uint64_t>(g_tc_wait_ns) : kTcWaitNs;
+  p.skip_tile = g_tc_skip_tile > 0 ? g_tc_skip_tile - 1 : -1;
+  p.sink = error_sink();
   p.n_tiles = n_groups * p.tpg;
   uint32_t off = 0;
   p.off_stage = off; off += nstage * stage_bytes;   // 1024-aligned sizes first
@@ -770,6 +786,12 @@ int launch_vq_assign_tc(const void* keys, int key_dtype, int64_t n_groups, int64
 }  // namespace ss
 
 using namespace ss;
+
+extern "C" int ss_set_assign_wait(int64_t wait_limit_ns, int64_t skip_tile) {
+  g_tc_wait_ns.store(wait_limit_ns);
+  g_tc_skip_tile.store(skip_tile);
+  return SS_OK;
+}
 
 extern "C" int ss_vq_assign_check(void* stream) {
   cudaError_t e = cudaStreamSynchronize(as_stream(stream));

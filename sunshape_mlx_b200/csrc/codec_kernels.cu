@@ -396,6 +396,28 @@ __global__ void __launch_bounds__(256) vq_scores_kernel(const float* q, int nq, 
   }
 }
 
+// ------------------------------------------------------------------ query x centroid table
+// out[q][b][c] = sum_j q[q][b * bd + j] * C[b][c][j] (fused multiply-adds in j
+// order). One thread per (q, b, c): consecutive threads write consecutive
+// centroids, so the table is written coalesced.
+__global__ void __launch_bounds__(256) query_centroid_dots_kernel(const float* q, int64_t nq, int d,
+                                                                  const float* cents, int bd, int k,
+                                                                  float* out) {
+  const int nb = d / bd;
+  const int64_t n = nq * nb * k;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t qi = e / ((int64_t)nb * k);
+    const int rem = static_cast<int>(e - qi * nb * k);
+    const int b = rem / k, c = rem - b * k;
+    const float* qq = q + qi * d + b * bd;
+    const float* cc = cents + ((size_t)b * k + c) * bd;
+    float acc = 0.f;
+    for (int j = 0; j < bd; ++j) acc = fmaf(__ldg(qq + j), __ldg(cc + j), acc);
+    out[e] = acc;
+  }
+}
+
 // ------------------------------------------------------------------ dequant
 __global__ void vq_dequant_kernel(const uint8_t* idx, int64_t n_groups, int64_t rpg,
                                   int64_t igs, int64_t irs, const float* cents, int d, int bd,
@@ -620,6 +642,21 @@ int ss_vq_scores(const float* q, int nq, int d, const float* centroids, int bd, 
                                                            d / bd, idx, t, idx_row_stride, out,
                                                            out_stride);
   return check_launch("ss_vq_scores");
+}
+
+int ss_query_centroid_dots(const float* q, int64_t nq, int d, const float* centroids, int bd,
+                           int k, float* out, void* stream) {
+  SS_REQUIRE(q && centroids && out, "ss_query_centroid_dots: null pointer");
+  SS_REQUIRE(nq >= 0 && bd > 0 && d % bd == 0 && k >= 1 && k <= 256,
+             "ss_query_centroid_dots: bad dims");
+  count_dispatch("ss_query_centroid_dots");
+  const int64_t n = nq * (d / bd) * k;
+  if (n == 0) return SS_OK;
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > (int64_t)sm_count() * 16) blocks = (int64_t)sm_count() * 16;
+  query_centroid_dots_kernel<<<static_cast<unsigned>(blocks), 256, 0, as_stream(stream)>>>(
+      q, nq, d, centroids, bd, k, out);
+  return check_launch("ss_query_centroid_dots");
 }
 
 int ss_vq_scores_lut(const float* qdots, int nq, int nb, int k, const uint8_t* idx, int64_t t,

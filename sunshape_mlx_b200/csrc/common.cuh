@@ -20,6 +20,8 @@ int fail(int code, const std::string& msg);      // records msg, returns code
 int check_launch(const char* what);              // cudaGetLastError -> status
 void count_dispatch(const char* name);
 int sm_count();                                  // of the current device
+// Device address of the process error sink (ss_set_error_sink), or null.
+int* error_sink();
 
 #define SS_REQUIRE(cond, msg)                                  \
   do {                                                         \
@@ -136,6 +138,14 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     if (mbar_try_wait(bar, parity)) return true;
     if (global_ns() - t0 > limit_ns) return false;
   }
+}
+
+// A bounded wait gave up: OR `code` into the launch's error word and, when a
+// process error sink is attached, into that host word (system scope, so the
+// host sees it without synchronizing).
+__device__ __forceinline__ void report_wait_failure(int* ws_err, int* sink, int code) {
+  if (ws_err) atomicOr(ws_err, code);
+  if (sink) atomicOr_system(sink, code);
 }
 
 // ---- bulk / tensor TMA (no cluster multicast anywhere in this library) ------

@@ -38,7 +38,7 @@ namespace {
 // values); one producer warp follows them.
 constexpr int kLutThreads = 256;  // table kernel block size
 constexpr int kMaxStages = 8;
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per barrier wait
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // default bound of a barrier wait (2 s)
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct DecodeParams {
@@ -97,6 +97,9 @@ struct DecodeParams {
   float* part_out;  // non-null: write (o, m, l) rows instead of the output
   // workspace
   int* err;
+  int* sink;                // process error sink (host word) or null
+  uint64_t wait_ns;         // bound of every barrier wait
+  int64_t skip_tile;        // test hook: tile whose copies are never issued (-1: none)
   int* counters;
   float* slots;
   float* lut_g;             // per-unit query x centroid tables [unit][nb][k][R]
@@ -433,9 +436,9 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
         }
         if (it > 0 && ++s == p.stages) { s = 0; ph ^= 1; }
         if (it >= p.stages) {
-          if (ms.abort || !mbar_wait_bounded(&empty_bar[s], ph ^ 1, kWaitLimitNs)) {
+          if (ms.abort || !mbar_wait_bounded(&empty_bar[s], ph ^ 1, p.wait_ns)) {
+            if (!ms.abort) report_wait_failure(p.err, p.sink, 1);
             ms.abort = 1;
-            atomicOr(p.err, 1);
             break;
           }
         }
@@ -447,6 +450,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
           else bytes += p.v_tile_bytes;
           if (p.n_heavy) bytes += TILE * p.n_heavy * p.bd * 2;
           mbar_arrive_expect_tx(&full_bar[s], bytes);
+          if (tau == p.skip_tile) continue;  // test hook: these bytes never arrive
           bulk_g2s(st + p.off_idx, p.idx + pair * p.idx_ps + t0 * p.nb, TILE * p.nb,
                    &full_bar[s]);
           uint8_t* aux = st + p.off_aux;
@@ -489,16 +493,17 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
           }
         }
       }
-      // Drain: make sure no copy issued by this CTA is still in flight.
+      // Drain: make sure no copy issued by this CTA is still in flight. Each
+      // stage is waited for separately (a stage whose bytes never arrive
+      // must not stop the wait for the others).
       const int issued = it;
+      bool drained = true;
       for (int j = issued - p.stages; j < issued; ++j) {
         if (j < 0) continue;
         const int s = j % p.stages;
-        if (!mbar_wait_bounded(&full_bar[s], (j / p.stages) & 1, kWaitLimitNs)) {
-          atomicOr(p.err, 2);
-          break;
-        }
+        if (!mbar_wait_bounded(&full_bar[s], (j / p.stages) & 1, p.wait_ns)) drained = false;
       }
+      if (!drained) report_wait_failure(p.err, p.sink, 2);
     }
     return;
   }
@@ -567,6 +572,8 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
 
   int64_t tau = t_begin;
   uint32_t unit_no = 0;
+  bool lut_out = false;     // thread 0: a table copy whose completion was not seen
+  uint32_t lut_phase = 0;
   while (tau < t_end) {
     const int64_t u = tau / p.tpu;
     const int64_t u_end = min(t_end, (u + 1) * p.tpu);
@@ -583,6 +590,12 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
       // Tables come from lut_kernel, launched just before as the primary of a
       // programmatic dependent launch: wait for its results once.
       if (unit_no == 0) grid_dependency_wait();
+    }
+    // after a give-up no further table copy is issued (so at most one, whose
+    // wait was skipped, can still be in flight: drained at the end)
+    if (ctid == 0 && !ms.abort) {
+      lut_out = true;
+      lut_phase = unit_no & 1;
       fence_proxy_async_smem();  // region was last written as merge scratch
       const uint32_t bytes = p.lut_unit_bytes;
       mbar_arrive_expect_tx(&lut_bar, bytes);
@@ -636,9 +649,13 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
         named_bar_sync(1, (CW * 32));
       }
     }
-    if (!ms.abort && !mbar_wait_bounded(&lut_bar, unit_no & 1, kWaitLimitNs)) {
-      ms.abort = 1;
-      atomicOr(p.err, 8);
+    if (!ms.abort) {
+      if (mbar_wait_bounded(&lut_bar, unit_no & 1, p.wait_ns)) {
+        lut_out = false;
+      } else {
+        ms.abort = 1;
+        report_wait_failure(p.err, p.sink, 8);
+      }
     }
     ++unit_no;
     uint32_t rok = 0;  // bit r: query row r of this unit exists
@@ -668,9 +685,9 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
         if (s >= p.stages) { s -= p.stages; ph ^= 1; }
       }
       const int lt = lt0 + i;
-      if (!ms.abort && !mbar_wait_bounded(&full_bar[s], ph, kWaitLimitNs)) {
+      if (!ms.abort && !mbar_wait_bounded(&full_bar[s], ph, p.wait_ns)) {
         ms.abort = 1;
-        atomicOr(p.err, 4);
+        report_wait_failure(p.err, p.sink, 4);
       }
       const bool aborted = ms.abort != 0;
       uint8_t* st = smem + (size_t)s * p.stage_bytes;
@@ -1206,6 +1223,10 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
     }
     tau = u_end;
   }
+  // a table copy still in flight after a give-up must land before the CTA
+  // exits (its shared memory is then handed to other CTAs)
+  if (ctid == 0 && lut_out && !mbar_wait_bounded(&lut_bar, lut_phase, p.wait_ns))
+    report_wait_failure(p.err, p.sink, 8);
 }
 
 // ------------------------------------------------------------------ merge
@@ -1447,7 +1468,8 @@ int launch_decode(const DecodeParams& p, const CUtensorMap& mv, const CUtensorMa
   return check_launch("ss_decode_attn");
 }
 
-int run_decode(const ss_decode_args* a, float* part_out, void* stream) {
+int run_decode(const ss_decode_args* a, float* part_out, void* stream,
+               const char* name = nullptr) {
   Plan pl;
   int rc = make_plan(a, pl);
   if (rc != SS_OK) return rc;
@@ -1542,6 +1564,9 @@ int run_decode(const ss_decode_args* a, float* part_out, void* stream) {
   p.part_out = part_out;
   uint8_t* ws = static_cast<uint8_t*>(a->workspace);
   p.err = reinterpret_cast<int*>(ws);
+  p.sink = error_sink();
+  p.wait_ns = a->wait_limit_ns > 0 ? static_cast<uint64_t>(a->wait_limit_ns) : kWaitLimitNs;
+  p.skip_tile = a->test_skip_tile > 0 ? a->test_skip_tile - 1 : -1;
   p.counters = reinterpret_cast<int*>(ws + pl.off_counters);
   p.slots = reinterpret_cast<float*>(ws + pl.off_slots);
   p.lut_g = reinterpret_cast<float*>(ws + pl.off_lut_g);
@@ -1549,7 +1574,7 @@ int run_decode(const ss_decode_args* a, float* part_out, void* stream) {
   p.stage_bytes = pl.stage_bytes; p.off_idx = pl.off_idx; p.off_aux = pl.off_aux;
   p.off_vdq = pl.off_vdq; p.off_lut = pl.off_lut; p.off_p = pl.off_p; p.off_misc = pl.off_misc;
   p.off_stage = 0;
-  count_dispatch(part_out ? "ss_decode_attn_partial" : "ss_decode_attn");
+  count_dispatch(name ? name : (part_out ? "ss_decode_attn_partial" : "ss_decode_attn"));
 #define SS_DISPATCH(RV, DV) \
   if (pl.R == RV && a->d == DV) return launch_decode<RV, DV>(p, mv, mvt, pl.smem, pl.cw, st);
   SS_DISPATCH(1, 128) SS_DISPATCH(2, 128) SS_DISPATCH(4, 128) SS_DISPATCH(8, 128)
@@ -1656,13 +1681,22 @@ extern "C" int ss_decode_attn_noalloc(const ss_decode_args* a, void* stream) {
   void* scratch = nullptr;
   rc = scratch_address(&scratch);
   if (rc != SS_OK) return rc;
-  // error word + arrival counters must start at zero; the array keeps the
-  // previous call's contents
-  cudaError_t e = cudaMemsetAsync(scratch, 0, pl.off_slots, as_stream(stream));
+  // the arrival counters must start at zero (the array keeps the previous
+  // call's contents); the error word before them stays sticky until
+  // ss_decode_noalloc_check reads it
+  cudaError_t e = cudaMemsetAsync(static_cast<uint8_t*>(scratch) + pl.off_counters, 0,
+                                  pl.off_slots - pl.off_counters, as_stream(stream));
   if (e != cudaSuccess)
     return fail(SS_ERR_CUDA, std::string("ss_decode_attn_noalloc: memset: ") + cudaGetErrorString(e));
   ss_decode_args b = *a;
   b.workspace = scratch;
   b.workspace_bytes = kNoAllocScratchBytes;
-  return run_decode(&b, nullptr, stream);
+  return run_decode(&b, nullptr, stream, "ss_decode_attn_noalloc");
+}
+
+extern "C" int ss_decode_noalloc_check(void* stream) {
+  void* scratch = nullptr;
+  const int rc = scratch_address(&scratch);
+  if (rc != SS_OK) return rc;
+  return ss_decode_check(scratch, stream);
 }

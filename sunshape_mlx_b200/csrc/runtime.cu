@@ -2,6 +2,7 @@
 // queries and a small cache of TMA tensor maps.
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <map>
@@ -36,6 +37,12 @@ void count_dispatch(const char* name) {
   std::lock_guard<std::mutex> lk(g_stats_mu);
   g_stats[name] += 1;
 }
+
+namespace {
+std::atomic<int*> g_error_sink{nullptr};
+}  // namespace
+
+int* error_sink() { return g_error_sink.load(std::memory_order_acquire); }
 
 int sm_count() {
   int dev = 0;
@@ -138,11 +145,27 @@ const CUtensorMap* tmap_3d_sw128(const void* base, int dtype, uint64_t inner, ui
 
 extern "C" {
 
-int ss_abi_version(void) { return 100; }
+int ss_abi_version(void) { return 101; }
 
 const char* ss_last_error(void) { return ss::g_last_error.c_str(); }
 
 int ss_device_sm_count(void) { return ss::sm_count(); }
+
+int ss_set_error_sink(int* host_word) {
+  if (!host_word) {
+    ss::g_error_sink.store(nullptr, std::memory_order_release);
+    return SS_OK;
+  }
+  void* dptr = nullptr;
+  cudaError_t e = cudaHostGetDevicePointer(&dptr, host_word, 0);
+  if (e != cudaSuccess || !dptr) {
+    cudaGetLastError();
+    return ss::fail(SS_ERR_BAD_ARG, std::string("ss_set_error_sink: not page-locked host memory "
+                                                "visible to the device: ") + cudaGetErrorString(e));
+  }
+  ss::g_error_sink.store(static_cast<int*>(dptr), std::memory_order_release);
+  return SS_OK;
+}
 
 int ss_kernel_stats(char* buf, size_t buf_len) {
   std::lock_guard<std::mutex> lk(ss::g_stats_mu);

@@ -78,6 +78,7 @@ def vq_assign(keys: torch.Tensor, centroids: torch.Tensor, *, perm: torch.Tensor
     keys may be a strided view with 2-level row layout (..., T, d); indices
     are written to ``out_idx`` (same leading shape, nb bytes per row).
     """
+    L.poll_device_errors()
     L.require_cuda(keys, centroids)
     nb, k, bd = centroids.shape
     d = keys.shape[-1]

@@ -42,7 +42,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_abi_version(lib):
-    assert lib.ss_abi_version() == 100
+    assert lib.ss_abi_version() == 101
 
 
 def test_decode_args_layout_matches_header():

@@ -146,3 +146,25 @@ def test_decode_schedule_partition():
         for u in range(nu):
             f, l = cta_of(s, u * tpu), cta_of(s, (u + 1) * tpu - 1)
             assert all(st[k + 1] > st[k] for k in range(f, l + 1))
+
+
+def test_deferred_tensor_computes_once_on_first_use():
+    """update_and_fetch's deferred keys: shape/dtype without computing; any
+    use computes once; torch functions and operators see the real tensor."""
+    import torch
+
+    from sunshape_mlx_b200.cache import DeferredTensor
+
+    calls = []
+
+    def fn():
+        calls.append(1)
+        return torch.arange(6, dtype=torch.float32).reshape(1, 1, 2, 3)
+
+    d = DeferredTensor(fn, (1, 1, 2, 3), torch.float32, torch.device("cpu"))
+    assert d.shape == (1, 1, 2, 3) and d.dtype == torch.float32 and d.ndim == 4
+    assert d.size(2) == 2 and not d.is_materialized and not calls
+    assert float((d * 2).sum()) == 30.0
+    assert torch.equal(torch.cat([d, d], 2)[0, 0, 2], torch.tensor([0.0, 1.0, 2.0]))
+    assert float(d[0, 0, 1, 2]) == 5.0 and d.float().shape == (1, 1, 2, 3)
+    assert d.is_materialized and len(calls) == 1

@@ -32,6 +32,7 @@ def test_noalloc_matches_workspace_entry_point(cuda_ok):
     v = torch.randn((B, HKV, cap, D), generator=g, device="cuda").half()
     lib = L.load()
     st = L.stream_ptr()
+    L.reset_kernel_stats()
     for step in range(2):
         q = torch.randn((B, HQ, 1, D), generator=g, device="cuda").half()
         spec = dict(tc=T - step * 700, cap=cap, idx=idx, v=v)
@@ -46,6 +47,12 @@ def test_noalloc_matches_workspace_entry_point(cuda_ok):
         torch.cuda.synchronize()
         assert not torch.isnan(out.float()).any()
         assert _rel(out, ref) < REL, (step, _rel(out, ref))
+    # no device-side wait gave up in either call (the error word of the fixed
+    # array is sticky; this reads and clears it), and the calls are counted
+    # under their own name
+    assert lib.ss_decode_noalloc_check(st) == L.SS_OK
+    stats = L.kernel_stats()
+    assert stats.get("ss_decode_attn_noalloc") == 2 and stats.get("ss_decode_attn") == 2
 
 
 def test_noalloc_rejects_oversized_problem(cuda_ok):
