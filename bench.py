@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Benchmark: fused SunShape decode attention.
+"""Benchmark: fused SunShape decode attention (batched GQA decode, 16 x 8192 tokens).
 
 Workload (per GPU): batch 16, 32 query heads / 8 kv heads, head_dim 128,
 T_kv = 8192 cached tokens per sequence; keys 1-bit SunShape block-VQ
@@ -718,7 +718,7 @@ def run_assign(args):
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "peak_source": peak_kind,
                      "note": "algorithmic 2*256*128 FLOP per token-head; the kernel is bound by "
-                             "its CUDA-core epilogue (profiles/vq_assign_tc_cfg2_cache_fill.md)"},
+                             "its CUDA-core epilogue (see the committed ncu summary of this kernel)"},
         "gpu_launches": args.steps,
         "clocks": clocks,
         "cpu_baseline": {"value": cpu_v, "unit": "token-heads/s", "cores": os.cpu_count(),
@@ -849,7 +849,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--config", type=int, choices=[2, 3, 4, 5], default=2,
-                    help="decode configuration (BASELINE configs 2, 3, 5; 4 = config-4 attention)")
+                    help="decode workload: 2 batched 8192-token decode, 3 TurboQuant-value 32768-token decode, 4 32-layer block-VQ K/V attention, 5 524288-token split-KV decode")
     ap.add_argument("--model", action="store_true",
                     help="with --config 4: the end-to-end decoder (tokens/s) instead of attention alone")
     ap.add_argument("--assign", action="store_true",

@@ -571,7 +571,8 @@ def tq_dequantize(packed, norms, rotation, bits: int, d: int):
 
 
 def tq_group_quantize(values, rotation, bits: int, group_size: int):
-    """Per-group-scaled TurboQuant (BASELINE config 3 format, an extension of
+    """Per-group-scaled TurboQuant (fp16 scale per group of channels, the value
+    format of the 32768-token decode workload; an extension of
     value_codecs.py:159-171): r = v @ R^T; per group of ``group_size``
     channels s = fp16(||r_g|| / sqrt(group_size)); idx = #{j : r > B_j * s}
     with the unscaled N(0,1) boundaries B; 2-bit packed as kernels.py:1102."""

@@ -69,6 +69,7 @@ struct DecodeParams {
   const uint32_t* vq;
   int64_t vq_ps;
   int v_bits, v_group, v_words, v_groups;
+  int v_gshift;              // log2(v_group) when a power of two, else -1
   const void* vs;
   int vs_dt;
   int64_t vs_ps;
@@ -106,6 +107,7 @@ struct DecodeParams {
   uint32_t lut_unit_bytes;
   // shared-memory carve-up (bytes from the 1024-aligned base)
   uint32_t off_stage, stage_bytes, off_idx, off_aux, off_vdq, off_lut, off_p, off_misc, off_vtab;
+  uint32_t off_plo;  // 8-row units: per-warp lo-half P slices (0: in the query rows of Misc)
 };
 
 // Tokens per consumer-warp slice (one per lane). With 128-token tiles this
@@ -397,6 +399,22 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
   const int64_t t_begin = range_start(sched, cta);
   const int64_t t_end = range_start(sched, cta + 1);
 
+  if (p.vfmt == SS_V_QUANT && p.v_bits == 2) {
+    // levels of the four 2-bit codes of every byte value as fp16 hi + lo
+    // pairs (level = hi + lo to about 2^-22)
+    uint4* lv4 = reinterpret_cast<uint4*>(smem + p.off_vtab);
+    for (int i = tid; i < 256; i += blockDim.x) {
+      float l[4], h[4], o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        l[j] = p.levels[(i >> (2 * j)) & 3];
+        h[j] = __half2float(__float2half_rn(l[j]));
+        o[j] = l[j] - h[j];
+      }
+      lv4[i] = make_uint4(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]), pack_h2(o[0], o[1]),
+                          pack_h2(o[2], o[3]));
+    }
+  }
   if (tid == 0) {
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(&full_bar[s], 1);
@@ -412,6 +430,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
     }
     for (int i = 0; i < 16; ++i) ms.levels[i] = p.levels[i];
     for (int i = 0; i < 16; ++i) ms.lvpair[i] = make_float2(p.levels[i & 3], p.levels[i >> 2]);
+
     fence_mbar_init();
   }
   __syncthreads();
@@ -519,9 +538,19 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
   const int wgroup = warp / wps, slice = warp % wps;
   const int ctid = tid;                        // 0..255
   const int64_t q_off = p.tc + p.ttail - p.tq;
+  // Softmax weights go to the P.V MMA as fp16 hi + lo pairs (p = hi + lo to
+  // about 2^-22 relative), so the weighted sum has fp32-level accuracy. With
+  // R <= 4 rows the lo halves sit in columns 4..7 of the same 8-column slice
+  // (one MMA computes both; the two column halves are added at the unit
+  // end); with 8 rows they have a slice of their own and a second MMA.
   __half* Pw = reinterpret_cast<__half*>(smem + p.off_p) + warp * SL * 8;  // [32][8]
+  __half* Pw_lo = R == 8 ? reinterpret_cast<__half*>(p.off_plo ? smem + p.off_plo
+                                                               : reinterpret_cast<uint8_t*>(&ms.qo[0][0])) +
+                               warp * SL * 8
+                         : Pw;
   uint8_t* vdq_w = smem + p.off_vdq + warp * (16 * D * 2);
   const uint32_t pw_addr = smem_u32(Pw) + (lane & 15) * 16;
+  const uint32_t pwl_addr = smem_u32(Pw_lo) + (lane & 15) * 16;
   // ldmatrix.x4.trans addressing: lane -> (8x8 matrix mi, row mj)
   const int mi = lane >> 3, mj = lane & 7;
   const int kk_off = (mi >= 2 ? 8 : 0) + mj;   // token row within a 16-token k-step
@@ -532,9 +561,11 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
   for (int m = 0; m < 4; ++m) swz[m] = static_cast<uint32_t>(((2 * m + dsel) ^ mj) << 4);
   const int rows_valid = p.nrep * p.tq;
   const bool per_token_mask = p.causal || p.mask != nullptr;
-  // columns R..7 of every P slice stay zero
-  for (int e = lane; e < SL * 8; e += 32)
-    if ((e & 7) >= R) Pw[e] = __float2half_rn(0.f);
+  // columns of every P slice that no row uses stay zero
+  if constexpr (R < 4) {
+    for (int e = lane; e < SL * 8; e += 32)
+      if ((e & 3) >= R) Pw[e] = __float2half_rn(0.f);
+  }
 
   // Heavy (fp16 pass-through) blocks score on warp MMAs when their dims fit
   // 16-dim k-steps: A = 16 tokens x 16 heavy dims straight from the stage,
@@ -855,7 +886,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
 
       // 2. online softmax over this warp's slice
       float alpha[R];
-      __half ph0[R], ph1[R];
+      __half ph0[R], pl0[R];
 #pragma unroll
       for (int r = 0; r < R; ++r) {
         const float mx = warp_max_f32(TPL > 1 ? fmaxf(s0[r], s1[r]) : s0[r]);
@@ -868,32 +899,31 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
           p0 = fast_exp2((s0[r] - mn) * kLog2e);
           p1 = fast_exp2((s1[r] - mn) * kLog2e);
         }
-        const __half h0 = __float2half_rn(p0), h1 = __float2half_rn(p1);
+        (void)p1;
+        const __half h0 = __float2half_rn(p0);
         ph0[r] = h0;
-        ph1[r] = h1;
-        l_l[r] = l_l[r] * alpha[r] + (__half2float(h0) + (TPL > 1 ? __half2float(h1) : 0.f));
+        pl0[r] = __float2half_rn(p0 - __half2float(h0));
+        l_l[r] = l_l[r] * alpha[r] + p0;
         m_w[r] = mn;
       }
-      // this lane's weights for all rows in one store per token
-      if constexpr (HV && R == 4 && TPL == 1) {
-        // full 16-byte row: columns 4..7 rewritten as zero (the heavy-block
-        // scratch may have used them)
+      // this lane's weights (hi and lo halves) for all rows
+      static_assert(TPL == 1, "one token per lane");
+      if constexpr (R == 4) {
         *reinterpret_cast<uint4*>(Pw + lane * 8) =
-            make_uint4(pack_halves2(ph0[0], ph0[1]), pack_halves2(ph0[2], ph0[3]), 0u, 0u);
-      } else if constexpr (R == 4 || R == 8) {
-#pragma unroll
-        for (int r4 = 0; r4 < R; r4 += 4) {
-          *reinterpret_cast<uint2*>(Pw + lane * 8 + r4) =
-              make_uint2(pack_halves2(ph0[r4], ph0[r4 + 1]), pack_halves2(ph0[r4 + 2], ph0[r4 + 3]));
-          if (TPL > 1)
-            *reinterpret_cast<uint2*>(Pw + (lane + 32) * 8 + r4) =
-                make_uint2(pack_halves2(ph1[r4], ph1[r4 + 1]), pack_halves2(ph1[r4 + 2], ph1[r4 + 3]));
-        }
+            make_uint4(pack_halves2(ph0[0], ph0[1]), pack_halves2(ph0[2], ph0[3]),
+                       pack_halves2(pl0[0], pl0[1]), pack_halves2(pl0[2], pl0[3]));
+      } else if constexpr (R == 8) {
+        *reinterpret_cast<uint4*>(Pw + lane * 8) =
+            make_uint4(pack_halves2(ph0[0], ph0[1]), pack_halves2(ph0[2], ph0[3]),
+                       pack_halves2(ph0[4], ph0[5]), pack_halves2(ph0[6], ph0[7]));
+        *reinterpret_cast<uint4*>(Pw_lo + lane * 8) =
+            make_uint4(pack_halves2(pl0[0], pl0[1]), pack_halves2(pl0[2], pl0[3]),
+                       pack_halves2(pl0[4], pl0[5]), pack_halves2(pl0[6], pl0[7]));
       } else {
 #pragma unroll
         for (int r = 0; r < R; ++r) {
           Pw[lane * 8 + r] = ph0[r];
-          if (TPL > 1) Pw[(lane + 32) * 8 + r] = ph1[r];
+          Pw[lane * 8 + 4 + r] = pl0[r];
         }
       }
       // The running maxima rarely move after the first tiles: rescale the
@@ -902,7 +932,8 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
 #pragma unroll
       for (int r = 0; r < R; ++r) moved = moved || alpha[r] != 1.f;
       if (moved) {
-        const int n0 = 2 * (lane & 3);
+        // column n holds row n (and, for R <= 4, row n - 4's lo half)
+        const int n0 = R == 8 ? 2 * (lane & 3) : (2 * (lane & 3)) & 3;
         float a0 = 1.f, a1 = 1.f;
 #pragma unroll
         for (int r = 0; r < R; ++r) {
@@ -921,13 +952,15 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
         const uint32_t vb = smem_u32(st) + (slice * SL + kk_off) * 128;
 #pragma unroll
         for (int ks = 0; ks < SL / 16; ++ks) {
-          uint32_t b0, b1;
+          uint32_t b0, b1, c0 = 0, c1 = 0;
           ldsm_x2_trans(pw_addr + ks * 256, b0, b1);
+          if constexpr (R == 8) ldsm_x2_trans(pwl_addr + ks * 256, c0, c1);
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt) {
             const uint32_t col = (mt >> 2) * (TILE * 128) + swz[mt & 3];
             uint32_t x0, x1, x2, x3;
             ldsm_x4_trans(vb + ks * 2048 + col, x0, x1, x2, x3);
+            if constexpr (R == 8) mma_16816(acc[mt], x0, x1, x2, x3, c0, c1);
             mma_16816(acc[mt], x0, x1, x2, x3, b0, b1);
           }
         }
@@ -935,9 +968,43 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
         const uint32_t vb = smem_u32(vdq_w) + kk_off * 128;
         for (int ks = 0; ks < SL / 16; ++ks) {
           // decode 16 tokens of the slice into this warp's fp16 staging tile
-          if (compressed && p.vfmt == SS_V_QUANT && D == 128 && p.v_bits == 2 && p.v_group % 16 == 0) {
-            // 2-bit codes: lane = (token, half row); four 16-value words per
-            // lane in one 16-byte load, one nibble -> two levels per lookup
+          if (compressed && p.vfmt == SS_V_QUANT && D == 128 && p.v_bits == 2 && p.v_gshift >= 4 &&
+              p.vs_dt == SS_F16 && !p.vz) {
+            // 2-bit codes with fp16 scales per power-of-two group (>= 16
+            // channels): lane = (token, half row); four 16-value words per lane
+            // in one 16-byte load; each code byte -> the hi/lo fp16 levels of
+            // its four codes by one table lookup; v = hi * s + (lo * s) in
+            // fp16 pairs, one rounding of the exact product as in fp32
+            const uint16_t* sp = reinterpret_cast<const uint16_t*>(st + p.off_aux + TILE * p.v_words * 4);
+            const uint4* lv4 = reinterpret_cast<const uint4*>(smem + p.off_vtab);
+            const int tk = lane >> 1, hw = lane & 1;
+            const int tt = slice * SL + ks * 16 + tk;
+            const uint4 wv = *reinterpret_cast<const uint4*>(st + p.off_aux + (tt * 8 + hw * 4) * 4);
+            const uint32_t wrd[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi) {
+              const int w = hw * 4 + wi;  // dims 16w .. 16w + 15
+              const uint16_t su = sp[tt * p.v_groups + ((w * 16) >> p.v_gshift)];
+              const __half2 sh = __halves2half2(__ushort_as_half(su), __ushort_as_half(su));
+              uint32_t h[8];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const uint4 e = lv4[__byte_perm(wrd[wi], 0u, 0x4440u + j)];
+                const __half2 l0 = __hmul2(*reinterpret_cast<const __half2*>(&e.z), sh);
+                const __half2 l1 = __hmul2(*reinterpret_cast<const __half2*>(&e.w), sh);
+                const __half2 a = __hfma2(*reinterpret_cast<const __half2*>(&e.x), sh, l0);
+                const __half2 b = __hfma2(*reinterpret_cast<const __half2*>(&e.y), sh, l1);
+                h[2 * j] = *reinterpret_cast<const uint32_t*>(&a);
+                h[2 * j + 1] = *reinterpret_cast<const uint32_t*>(&b);
+              }
+              *reinterpret_cast<uint4*>(vdq_w + vtile_addr(0, 16, tk, w * 16)) =
+                  make_uint4(h[0], h[1], h[2], h[3]);
+              *reinterpret_cast<uint4*>(vdq_w + vtile_addr(0, 16, tk, w * 16 + 8)) =
+                  make_uint4(h[4], h[5], h[6], h[7]);
+            }
+          } else if (compressed && p.vfmt == SS_V_QUANT && D == 128 && p.v_bits == 2 && p.v_group % 16 == 0) {
+            // 2-bit codes with fp32 scales (and zeros): lane = (token, half
+            // row); one nibble -> two levels per lookup, fp32 arithmetic
             const uint8_t* sp = st + p.off_aux + TILE * p.v_words * 4;
             const float* zp = p.vz ? reinterpret_cast<const float*>(
                                          sp + TILE * p.v_groups * (p.vs_dt == SS_F32 ? 4 : 2))
@@ -949,7 +1016,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
 #pragma unroll
             for (int wi = 0; wi < 4; ++wi) {
               const int w = hw * 4 + wi;  // dims 16w .. 16w + 15
-              const int gi = (w * 16) / p.v_group;
+              const int gi = p.v_gshift >= 0 ? (w * 16) >> p.v_gshift : (w * 16) / p.v_group;
               const float s_ = p.vs_dt == SS_F32
                                    ? reinterpret_cast<const float*>(sp)[tt * p.v_groups + gi]
                                    : h2f(reinterpret_cast<const uint16_t*>(sp)[tt * p.v_groups + gi]);
@@ -1054,13 +1121,15 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
             }
           }
           __syncwarp();
-          uint32_t b0, b1;
+          uint32_t b0, b1, c0 = 0, c1 = 0;
           ldsm_x2_trans(pw_addr + ks * 256, b0, b1);
+          if constexpr (R == 8) ldsm_x2_trans(pwl_addr + ks * 256, c0, c1);
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt) {
             const uint32_t col = (mt >> 2) * (16 * 128) + ((((2 * mt + dsel) & 7) ^ mj) << 4);
             uint32_t x0, x1, x2, x3;
             ldsm_x4_trans(vb + col, x0, x1, x2, x3);
+            if constexpr (R == 8) mma_16816(acc[mt], x0, x1, x2, x3, c0, c1);
             mma_16816(acc[mt], x0, x1, x2, x3, b0, b1);
           }
           __syncwarp();
@@ -1087,6 +1156,13 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
     // merge weights (per warp, or per cross-CTA partial, and row)
     float (*mo)[D] = reinterpret_cast<float (*)[D]>(lut + CW * R * (D + 2));
     float* wt = lut + CW * R * (D + 2) + R * D;
+    if constexpr (R <= 4) {
+      // add the lo-half columns 4..7 (lanes t + 2) to their rows' columns
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[mt][i] += __shfl_xor_sync(0xffffffffu, acc[mt][i], 2);
+    }
     {
       const int n0 = 2 * (lane & 3);
       const int m0 = lane >> 2;
@@ -1269,6 +1345,7 @@ struct Plan {
   int R, cw, tile, n_rg, n_ct, n_tt, tpu, grid, stages, max_cov, v_words, v_groups, w_unit;
   int64_t total_tiles, n_units;
   uint32_t stage_bytes, off_idx, off_aux, off_vdq, off_lut, off_p, off_misc, off_vtab, v_tile_bytes;
+  uint32_t off_plo;
   size_t smem;
   size_t ws_bytes, off_counters, off_slots, off_lut_g, lut_unit_bytes;
 };
@@ -1354,7 +1431,9 @@ int make_plan_r(const ss_decode_args* a, Plan& pl, int r_cap, int cw) {
   // per-warp fp16 value slices (16 tokens) for the quantized path
   const size_t vdq = (a->vfmt != SS_V_F16) ? (size_t)cw * 16 * a->d * 2 : 0;
   // VQ value centroids [nb_v][256][bd_v] fp16, resident for the whole launch
-  const size_t vtab = (a->vfmt == SS_V_VQ) ? (size_t)a->d * 256 * 2 : 0;
+  // (2-bit quantized values: a 4 KB table of the levels of every code byte)
+  const size_t vtab = (a->vfmt == SS_V_VQ) ? (size_t)a->d * 256 * 2
+                      : (a->vfmt == SS_V_QUANT && a->v_bits == 2) ? 4096 : 0;
   // the LUT region doubles as the per-warp merge scratch at unit ends
   size_t lut = (size_t)nb * a->k * R * 4;
   // per-warp merge scratch + the merged rows of the unit + merge weights
@@ -1362,7 +1441,13 @@ int make_plan_r(const ss_decode_args* a, Plan& pl, int r_cap, int cw) {
   const size_t n_wt = std::max<size_t>((size_t)cw, (size_t)pl.max_cov);
   const size_t scratch = (size_t)cw * R * (a->d + 2) * 4 + (size_t)R * a->d * 4 + n_wt * R * 4;
   if (lut < scratch) lut = scratch;
-  const size_t pbytes = (size_t)cw * slice_tokens(R) * 16;  // per-warp P slice [tokens][8] fp16
+  size_t pbytes = (size_t)cw * slice_tokens(R) * 16;  // per-warp P slice [tokens][8] fp16
+  // 8-row units keep the lo halves of P in a second slice per warp: in the
+  // unit's query rows of Misc (4 KB, free during the tile loop when there is
+  // no fp16 tail to score), else in a region of their own
+  const bool plo_own = R == 8 && (a->ttail > 0 || (size_t)cw * slice_tokens(R) * 16 > sizeof(float) * 8 * 128);
+  const size_t plo = plo_own ? pbytes : 0;
+  pbytes += plo;
   fixed = vdq + vtab + ((lut + 127) & ~size_t(127)) + pbytes + ((sizeof(Misc) + 127) & ~size_t(127)) + 1024;
   if (fixed + 2 * (size_t)pl.stage_bytes > kSmemBudget)
     return fail(SS_ERR_UNSUPPORTED, "ss_decode_attn: configuration exceeds shared memory");
@@ -1386,6 +1471,7 @@ int make_plan_r(const ss_decode_args* a, Plan& pl, int r_cap, int cw) {
   pl.off_lut = static_cast<uint32_t>(off);
   off += (lut + 127) & ~size_t(127);
   pl.off_p = static_cast<uint32_t>(off);
+  pl.off_plo = plo_own ? static_cast<uint32_t>(off + (pbytes - plo)) : 0u;
   off += pbytes;
   pl.off_misc = static_cast<uint32_t>(off);
   off += (sizeof(Misc) + 127) & ~size_t(127);
@@ -1549,6 +1635,9 @@ int run_decode(const ss_decode_args* a, float* part_out, void* stream,
   p.idx = a->idx; p.idx_ps = a->idx_pair_stride;
   p.kheavy = a->kheavy; p.kh_ps = a->kheavy_pair_stride;
   p.vfmt = a->vfmt; p.v_ps = a->v_pair_stride; p.vq = a->vq; p.vq_ps = a->vq_pair_stride;
+  p.v_gshift = -1;
+  for (int sh = 0; sh < 12; ++sh)
+    if (a->v_group == (1 << sh)) p.v_gshift = sh;
   p.v_bits = a->v_bits; p.v_group = a->v_group; p.v_words = pl.v_words; p.v_groups = pl.v_groups;
   p.vs = a->v_scales; p.vs_dt = a->v_scale_dtype; p.vs_ps = a->vs_pair_stride;
   p.vz = a->v_zeros; p.vz_ps = a->vz_pair_stride;
@@ -1573,6 +1662,7 @@ int run_decode(const ss_decode_args* a, float* part_out, void* stream,
   p.lut_unit_bytes = static_cast<uint32_t>(pl.lut_unit_bytes);
   p.stage_bytes = pl.stage_bytes; p.off_idx = pl.off_idx; p.off_aux = pl.off_aux;
   p.off_vdq = pl.off_vdq; p.off_lut = pl.off_lut; p.off_p = pl.off_p; p.off_misc = pl.off_misc;
+  p.off_plo = pl.off_plo;
   p.off_stage = 0;
   count_dispatch(name ? name : (part_out ? "ss_decode_attn_partial" : "ss_decode_attn"));
 #define SS_DISPATCH(RV, DV) \

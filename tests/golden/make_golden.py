@@ -1,9 +1,8 @@
 """Generate golden vectors by running the REFERENCE package's own code.
 
-Run in a container that has the reference tree (default
-``/root/reference``; override with ``SUNSHAPE_REF=<path>``):
+Run where the reference tree is available, naming its root directory:
 
-    python tests/golden/make_golden.py
+    SUNSHAPE_REF=<path to the reference tree> python tests/golden/make_golden.py
 
 The reference imports ``mlx.core``; MLX is not installable here, so
 ``mlx_numpy_shim.py`` is put in its place. Every Metal wrapper then takes its
@@ -49,7 +48,9 @@ def _save(name: str, **arrays):
 
 
 def main():
-    ref_root = os.environ.get("SUNSHAPE_REF", "/root/reference")
+    ref_root = os.environ.get("SUNSHAPE_REF")
+    if not ref_root:
+        raise SystemExit("set SUNSHAPE_REF to the root of the reference tree")
     ss = _import_reference(ref_root)
     from sunshape_mlx.codec import SunShapeBlockCodec
     from sunshape_mlx import kernels as K
