@@ -572,6 +572,9 @@ def run_config(args, world, rank, local):
     if world > 1:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     ms = float(ms_t)
+    phases = None
+    if world > 1 and args.config == 5:
+        phases = _splitkv_phases(q, cache, scale, args.steps, device)
     if rank != 0:
         return None
     peak, peak_kind = _peaks()
@@ -599,9 +602,38 @@ def run_config(args, world, rank, local):
         "gpu_launches": launches * args.steps,
         "clocks": clocks,
     }
+    if phases is not None:
+        line["splitkv_phases_ms"] = phases
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = _cpu_baseline_cfg(args.config, codec, cache, q)
     return line
+
+
+def _splitkv_phases(q, cache, scale, steps, device):
+    """Per-phase device time of the split-KV step (this rank's fused decode
+    partials, the NCCL all-gather, the log-sum-exp merge), CUDA events around
+    each phase, averaged over `steps` steps, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from sunshape_mlx_b200 import splitkv
+    from sunshape_mlx_b200.attention import decode_partials
+
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+    dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(steps):
+        ev[i][0].record()
+        part = decode_partials(q, cache, scale)
+        ev[i][1].record()
+        parts = splitkv.all_gather_partials(part)
+        ev[i][2].record()
+        splitkv.merge_partials(parts, q.shape, q.dtype)
+        ev[i][3].record()
+    torch.cuda.synchronize()
+    t = torch.tensor([[e[k].elapsed_time(e[k + 1]) for k in range(3)] for e in ev],
+                     dtype=torch.float64, device=device).mean(0)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return {"decode_partials": float(t[0]), "all_gather": float(t[1]), "lse_merge": float(t[2])}
 
 
 def _cpu_baseline_cfg(cfg, codec, cache, q, budget_s: float = 8.0):
@@ -802,42 +834,113 @@ def run_encode(args):
 
 
 # ---------------------------------------------------------------------- reference arm
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def _import_reference():
+    """The unmodified reference package from baseline/_ref, with the NumPy
+    stand-in for ``mlx.core`` (MLX has no Linux build here): every Metal
+    wrapper then takes its own fallback, i.e. the reference's CPU path."""
+    import types
+
+    if not os.path.isdir(os.path.join(REF_DIR, "sunshape_mlx")):
+        return None
+    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+    import mlx_numpy_shim
+
+    pkg = types.ModuleType("mlx")
+    pkg.core = mlx_numpy_shim
+    sys.modules.setdefault("mlx", pkg)
+    sys.modules.setdefault("mlx.core", mlx_numpy_shim)
+    sys.path.insert(0, REF_DIR)
+    import sunshape_mlx
+
+    return sunshape_mlx
+
+
 def run_reference(args):
-    """The reference's CPU path (oracle port of its NumPy quantize loop and
-    2-pass SDPA) on the host cores, one batch row of the workload per step."""
+    """The reference's own decode step on the host cores: its codec fit on
+    the workload's calibration set, its SunShapeKVCache filled with one batch
+    row (8 kv-heads x 8192 tokens, its NumPy quantize loop), then per step the
+    mlx-lm call order -- update_and_fetch of one new token (which dequantizes
+    the whole key cache, cache.py:205) and sunshape_sdpa (its per-query-head
+    loop, attention.py:268-352) -- followed by trim(1) so every step sees
+    8192 + 1 tokens. Beside it, the NumPy restatement of the same SDPA (the
+    oracle port) on the same inputs, as cpu_baseline.port."""
     import oracle as O
 
+    ref = _import_reference()
     qc, kc, sig = _calibration()
-    st = O.fit(qc.astype(np.float32), kc.astype(np.float32), head_dim=D, block_dim=BD,
-               n_centroids=KC, kmeans_iters=25, seed=0)
     rng = np.random.default_rng(12345)
     keys = (rng.standard_normal((1, HKV, T, D)).astype(np.float32) * sig).astype(np.float16)
     vals = rng.standard_normal((1, HKV, T, D)).astype(np.float16)
+    q = rng.standard_normal((1, HQ, 1, D)).astype(np.float16)
+    knew = (rng.standard_normal((1, HKV, 1, D)).astype(np.float32) * sig).astype(np.float16)
+    vnew = rng.standard_normal((1, HKV, 1, D)).astype(np.float16)
+    scale = 1 / math.sqrt(D)
+    port = None
+    if ref is None:
+        kind, why = "port", "baseline/_ref missing: NumPy restatement of the reference's CPU path"
+    else:
+        from sunshape_mlx.attention import sunshape_sdpa
+        from sunshape_mlx.cache import create_kv_cache
+        from sunshape_mlx.codec import SunShapeBlockCodec
+
+        codec = SunShapeBlockCodec(head_dim=D, block_dim=BD, n_centroids=KC)
+        codec.fit(qc.astype(np.float32), kc.astype(np.float32), kmeans_iters=25, seed=0)
+        cache = create_kv_cache(codec, n_kv_heads=HKV)
+        cache.update_and_fetch(keys, vals)
+
+        def step():
+            cache.update_and_fetch(knew, vnew)
+            out = sunshape_sdpa(q, cache, scale)
+            cache.trim(1)
+            return out
+        kind, why = "reference", ("the reference package (baseline/_ref) over a NumPy stand-in for "
+                                  "mlx.core: its CPU fallback paths")
+    # the oracle port on the same inputs (the arm itself without baseline/_ref)
+    st = O.fit(qc.astype(np.float32), kc.astype(np.float32), head_dim=D, block_dim=BD,
+               n_centroids=KC, kmeans_iters=25, seed=0)
     idx = np.zeros((1, HKV, T, NB), np.uint8)
     for h in range(HKV):
         for a in range(0, T, 2048):
             idx[0, h, a:a + 2048] = O.quantize(st, keys[0, h, a:a + 2048].astype(np.float32))[0]
-    q = rng.standard_normal((1, HQ, 1, D)).astype(np.float16)
+
+    def port_step():
+        return O.sdpa(q, st, idx, vals, scale)
+    if ref is None:
+        step = port_step
     for _ in range(max(1, args.warmup)):
-        O.sdpa(q, st, idx, vals, 1 / math.sqrt(D))
+        step()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        O.sdpa(q, st, idx, vals, 1 / math.sqrt(D))
+        step()
     dt = (time.perf_counter() - t0) / args.steps
     v = HQ / dt
-    return {
+    if ref is not None:
+        port_step()
+        n, p0 = 0, time.perf_counter()
+        while n < 3 or time.perf_counter() - p0 < 5.0:
+            port_step()
+            n += 1
+        port = {"value": HQ * n / (time.perf_counter() - p0), "unit": "queries/s",
+                "cores": os.cpu_count(), "kind": "port",
+                "sample": "decode of 1 batch row through the oracle's NumPy restatement"}
+    line = {
         "metric": METRIC, "value": v, "unit": "queries/s", "impl": "reference", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded anisotropic keys, N(0,1) fp16 values/queries)",
         "config": {"workload": WORKLOAD, "global_batch": B, "seq_len": T,
                    "parallelism": "host CPU", "sample": "1 of 16 batch rows per step"},
-        "cpu_baseline": {"value": v, "unit": "queries/s", "cores": os.cpu_count(), "kind": "port",
-                         "sample": "per step: decode of 1 batch row (32 queries x 8 kv-heads x "
-                                   "8192 tokens) through the NumPy restatement of the reference's "
-                                   "CPU SDPA path (MLX is not installable here)"},
+        "cpu_baseline": {"value": v, "unit": "queries/s", "cores": os.cpu_count(), "kind": kind,
+                         "sample": "per step: update_and_fetch of 1 token + decode of 1 batch row "
+                                   "(32 queries x 8 kv-heads x 8193 tokens), " + why},
         "e2e": {"value": v, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if port is not None:
+        line["cpu_baseline_port"] = port
+    return line
 
 
 def main():
