@@ -511,6 +511,8 @@ def run_config(args, world, rank, local):
     from sunshape_mlx_b200 import splitkv
 
     c = {3: CFG3, 4: CFG4, 5: CFG5}[args.config]
+    if args.batch and args.config == 3:
+        c["B"] = args.batch
     layers = c.get("LAYERS", 1)
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
@@ -960,6 +962,8 @@ def main():
     ap.add_argument("--assign-path", choices=["tensor", "simt", "auto"], default="tensor")
     ap.add_argument("--encode", action="store_true",
                     help="benchmark the value encoders (config-3 value stream)")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="override the batch of --config 3 (smaller cases for profiling)")
     ap.add_argument("--profile", action="store_true",
                     help="build the workload, run warmup+steps decode launches, exit "
                          "(short command for ncu captures)")

@@ -399,22 +399,6 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
   const int64_t t_begin = range_start(sched, cta);
   const int64_t t_end = range_start(sched, cta + 1);
 
-  if (p.vfmt == SS_V_QUANT && p.v_bits == 2) {
-    // levels of the four 2-bit codes of every byte value as fp16 hi + lo
-    // pairs (level = hi + lo to about 2^-22)
-    uint4* lv4 = reinterpret_cast<uint4*>(smem + p.off_vtab);
-    for (int i = tid; i < 256; i += blockDim.x) {
-      float l[4], h[4], o[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        l[j] = p.levels[(i >> (2 * j)) & 3];
-        h[j] = __half2float(__float2half_rn(l[j]));
-        o[j] = l[j] - h[j];
-      }
-      lv4[i] = make_uint4(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]), pack_h2(o[0], o[1]),
-                          pack_h2(o[2], o[3]));
-    }
-  }
   if (tid == 0) {
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(&full_bar[s], 1);
@@ -968,43 +952,9 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
         const uint32_t vb = smem_u32(vdq_w) + kk_off * 128;
         for (int ks = 0; ks < SL / 16; ++ks) {
           // decode 16 tokens of the slice into this warp's fp16 staging tile
-          if (compressed && p.vfmt == SS_V_QUANT && D == 128 && p.v_bits == 2 && p.v_gshift >= 4 &&
-              p.vs_dt == SS_F16 && !p.vz) {
-            // 2-bit codes with fp16 scales per power-of-two group (>= 16
-            // channels): lane = (token, half row); four 16-value words per lane
-            // in one 16-byte load; each code byte -> the hi/lo fp16 levels of
-            // its four codes by one table lookup; v = hi * s + (lo * s) in
-            // fp16 pairs, one rounding of the exact product as in fp32
-            const uint16_t* sp = reinterpret_cast<const uint16_t*>(st + p.off_aux + TILE * p.v_words * 4);
-            const uint4* lv4 = reinterpret_cast<const uint4*>(smem + p.off_vtab);
-            const int tk = lane >> 1, hw = lane & 1;
-            const int tt = slice * SL + ks * 16 + tk;
-            const uint4 wv = *reinterpret_cast<const uint4*>(st + p.off_aux + (tt * 8 + hw * 4) * 4);
-            const uint32_t wrd[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-            for (int wi = 0; wi < 4; ++wi) {
-              const int w = hw * 4 + wi;  // dims 16w .. 16w + 15
-              const uint16_t su = sp[tt * p.v_groups + ((w * 16) >> p.v_gshift)];
-              const __half2 sh = __halves2half2(__ushort_as_half(su), __ushort_as_half(su));
-              uint32_t h[8];
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const uint4 e = lv4[__byte_perm(wrd[wi], 0u, 0x4440u + j)];
-                const __half2 l0 = __hmul2(*reinterpret_cast<const __half2*>(&e.z), sh);
-                const __half2 l1 = __hmul2(*reinterpret_cast<const __half2*>(&e.w), sh);
-                const __half2 a = __hfma2(*reinterpret_cast<const __half2*>(&e.x), sh, l0);
-                const __half2 b = __hfma2(*reinterpret_cast<const __half2*>(&e.y), sh, l1);
-                h[2 * j] = *reinterpret_cast<const uint32_t*>(&a);
-                h[2 * j + 1] = *reinterpret_cast<const uint32_t*>(&b);
-              }
-              *reinterpret_cast<uint4*>(vdq_w + vtile_addr(0, 16, tk, w * 16)) =
-                  make_uint4(h[0], h[1], h[2], h[3]);
-              *reinterpret_cast<uint4*>(vdq_w + vtile_addr(0, 16, tk, w * 16 + 8)) =
-                  make_uint4(h[4], h[5], h[6], h[7]);
-            }
-          } else if (compressed && p.vfmt == SS_V_QUANT && D == 128 && p.v_bits == 2 && p.v_group % 16 == 0) {
-            // 2-bit codes with fp32 scales (and zeros): lane = (token, half
-            // row); one nibble -> two levels per lookup, fp32 arithmetic
+          if (compressed && p.vfmt == SS_V_QUANT && D == 128 && p.v_bits == 2 && p.v_group % 16 == 0) {
+            // 2-bit codes: lane = (token, half row); four 16-value words per
+            // lane in one 16-byte load, one nibble -> two levels per lookup
             const uint8_t* sp = st + p.off_aux + TILE * p.v_words * 4;
             const float* zp = p.vz ? reinterpret_cast<const float*>(
                                          sp + TILE * p.v_groups * (p.vs_dt == SS_F32 ? 4 : 2))
@@ -1431,9 +1381,7 @@ int make_plan_r(const ss_decode_args* a, Plan& pl, int r_cap, int cw) {
   // per-warp fp16 value slices (16 tokens) for the quantized path
   const size_t vdq = (a->vfmt != SS_V_F16) ? (size_t)cw * 16 * a->d * 2 : 0;
   // VQ value centroids [nb_v][256][bd_v] fp16, resident for the whole launch
-  // (2-bit quantized values: a 4 KB table of the levels of every code byte)
-  const size_t vtab = (a->vfmt == SS_V_VQ) ? (size_t)a->d * 256 * 2
-                      : (a->vfmt == SS_V_QUANT && a->v_bits == 2) ? 4096 : 0;
+  const size_t vtab = (a->vfmt == SS_V_VQ) ? (size_t)a->d * 256 * 2 : 0;
   // the LUT region doubles as the per-warp merge scratch at unit ends
   size_t lut = (size_t)nb * a->k * R * 4;
   // per-warp merge scratch + the merged rows of the unit + merge weights
