@@ -141,6 +141,13 @@ int ss_vq_scores(const float* q, int nq, int d, const float* centroids, int bd, 
  * * centroids[b][c][j], q f32 (nq, d) contiguous, already in codec space. */
 int ss_query_centroid_dots(const float* q, int64_t nq, int d, const float* centroids, int bd,
                            int k, float* out, void* stream);
+/* Row transform out[r] = x[r] @ m (m f32 (d, d) row-major, fused
+ * multiply-adds in i order; x f32 rows of stride x_row_stride; out f32 / f16
+ * / bf16 rows of stride out_row_stride; d a power of two <= 128). Replaces
+ * the rotation products of rotated-mode codecs (codec.py:273-293) and of
+ * the TurboQuant value basis (value_codecs.py:159-177). */
+int ss_rotate_rows(const float* x, int64_t rows, int d, int64_t x_row_stride, const float* m,
+                   void* out, int out_dtype, int64_t out_row_stride, void* stream);
 /* Same gather from a precomputed table qdots f32 (nq, nb, k)
  * (block_vq_score_metal's input, kernels.py:87-116). */
 int ss_vq_scores_lut(const float* qdots, int nq, int nb, int k, const uint8_t* idx, int64_t t,

@@ -126,6 +126,7 @@ _SIGS = {
     "ss_set_error_sink": ([vp], i32),
     "ss_set_assign_wait": ([i64, i64], i32),
     "ss_query_centroid_dots": ([vp, i64, i32, vp, i32, i32, vp, vp], i32),
+    "ss_rotate_rows": ([vp, i64, i32, i64, vp, vp, i32, i64, vp], i32),
 }
 
 EXPORTED = tuple(_SIGS)

@@ -351,8 +351,7 @@ def _quantize_keys_into(codec: SunShapeBlockCodec, keys: torch.Tensor, idx_out: 
                         heavy_out: torch.Tensor | None) -> None:
     """Assigns (B, H, T, D) keys straight into a strided cache slice."""
     if codec.use_rotation:
-        from .rotation import _matmul_f32
-        keys = _matmul_f32(keys.float(), codec.rotation.T).contiguous()
+        keys = K.rotate_rows(keys, codec.rotation.T)
         perm = None
     else:
         perm = codec.permutation if codec._is_perm() else None
@@ -373,8 +372,7 @@ def _dequantize_keys(codec: SunShapeBlockCodec, idx: torch.Tensor,
                        heavy=codec.heavy_u8 if heavy_vals is not None else None,
                        heavy_vals=heavy_vals)
     if codec.use_rotation:
-        from .rotation import _matmul_f32
-        out = _matmul_f32(out, codec.rotation)
+        out = K.rotate_rows(out, codec.rotation)
     return out
 
 
@@ -554,9 +552,8 @@ class HybridSunShapeKVCache:
         self._value_buffer[:, :, b0:b0 + T] = v
         if self._value_buffer_rot is not None:
             if self.value_backend == "turboquant":
-                from .rotation import _matmul_f32
                 rt = self._value_codec_impl.rotation_t
-                self._value_buffer_rot[:, :, b0:b0 + T] = _matmul_f32(v.float(), rt).half()
+                self._value_buffer_rot[:, :, b0:b0 + T] = K.rotate_rows(v, rt, torch.float16)
             else:  # block-VQ values: the value codec's own basis
                 self._value_buffer_rot[:, :, b0:b0 + T] = \
                     self.value_codec._forward_transform(v.float()).half()

@@ -174,7 +174,7 @@ class SunShapeBlockCodec:
         if self._is_perm():
             return apply_permutation(x, self.permutation)
         if self.use_rotation:
-            return _matmul_f32(x, self.rotation.T)
+            return K.rotate_rows(x, self.rotation.T)
         return x
 
     def _inverse_transform(self, x: torch.Tensor) -> torch.Tensor:
@@ -182,7 +182,7 @@ class SunShapeBlockCodec:
         if self._is_perm():
             return apply_permutation(x, self.inv_permutation)
         if self.use_rotation:
-            return _matmul_f32(x, self.rotation)
+            return K.rotate_rows(x, self.rotation)
         return x
 
     @property
@@ -288,7 +288,7 @@ class SunShapeBlockCodec:
         if self._is_perm():
             perm = self.permutation
         elif self.use_rotation:
-            x = _matmul_f32(x.float(), self.rotation.T).contiguous()
+            x = K.rotate_rows(x, self.rotation.T)
         n = x.shape[0]
         pt = None
         if self.has_heavy:

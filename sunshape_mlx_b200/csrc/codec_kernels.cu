@@ -418,6 +418,50 @@ __global__ void __launch_bounds__(256) query_centroid_dots_kernel(const float* q
   }
 }
 
+// ------------------------------------------------------------------ row transform
+// out[r][j] = sum_i x[r][i] * m[i][j] (fused multiply-adds in i order), the
+// rotations of rotated-mode keys and of the TurboQuant fp16 tail. A CTA
+// holds m (d x d f32) and a tile of kRotRows rows in shared memory; thread
+// (column j, row group) accumulates kRotRows * blockDim / d rows.
+constexpr int kRotRows = 64;
+__global__ void __launch_bounds__(256) rotate_rows_kernel(const float* x, int64_t rows, int d,
+                                                          int64_t xs, const float* m, void* out,
+                                                          int odt, int64_t os) {
+  extern __shared__ float rsm[];
+  float* sm_m = rsm;              // [d][d]
+  float* sm_x = rsm + d * d;      // [kRotRows][d]
+  const int64_t r0 = (int64_t)blockIdx.x * kRotRows;
+  const int nr = rows - r0 < kRotRows ? static_cast<int>(rows - r0) : kRotRows;
+  for (int e = threadIdx.x; e < d * d; e += blockDim.x) sm_m[e] = m[e];
+  for (int e = threadIdx.x; e < nr * d; e += blockDim.x) {
+    const int rr = e / d, i = e - rr * d;
+    sm_x[e] = x[(r0 + rr) * xs + i];
+  }
+  __syncthreads();
+  const int j = threadIdx.x % d;
+  const int groups = blockDim.x / d;
+  const int g = threadIdx.x / d;
+  if (g >= groups) return;
+  constexpr int kMaxRpt = kRotRows;  // rows per thread at d = blockDim (upper bound)
+  const int rpt = kRotRows / groups;
+  float acc[kMaxRpt / 2];
+  for (int base = 0; base < rpt; base += kMaxRpt / 2) {
+    const int n = min(kMaxRpt / 2, rpt - base);
+#pragma unroll
+    for (int q = 0; q < kMaxRpt / 2; ++q) acc[q] = 0.f;
+    for (int i = 0; i < d; ++i) {
+      const float mv = sm_m[i * d + j];
+#pragma unroll
+      for (int q = 0; q < kMaxRpt / 2; ++q)
+        if (q < n) acc[q] = fmaf(sm_x[(g * rpt + base + q) * d + i], mv, acc[q]);
+    }
+    for (int q = 0; q < n; ++q) {
+      const int rr = g * rpt + base + q;
+      if (rr < nr) store_from_f32(out, odt, (r0 + rr) * os + j, acc[q]);
+    }
+  }
+}
+
 // ------------------------------------------------------------------ dequant
 __global__ void vq_dequant_kernel(const uint8_t* idx, int64_t n_groups, int64_t rpg,
                                   int64_t igs, int64_t irs, const float* cents, int d, int bd,
@@ -657,6 +701,21 @@ int ss_query_centroid_dots(const float* q, int64_t nq, int d, const float* centr
   query_centroid_dots_kernel<<<static_cast<unsigned>(blocks), 256, 0, as_stream(stream)>>>(
       q, nq, d, centroids, bd, k, out);
   return check_launch("ss_query_centroid_dots");
+}
+
+int ss_rotate_rows(const float* x, int64_t rows, int d, int64_t x_row_stride, const float* m,
+                   void* out, int out_dtype, int64_t out_row_stride, void* stream) {
+  SS_REQUIRE(x && m && out, "ss_rotate_rows: null pointer");
+  SS_REQUIRE(d >= 1 && d <= 128 && 256 % d == 0 && rows >= 0,
+             "ss_rotate_rows: d must be a power of two <= 128");
+  count_dispatch("ss_rotate_rows");
+  if (rows == 0) return SS_OK;
+  const size_t smem = ((size_t)d * d + (size_t)kRotRows * d) * sizeof(float);
+  cudaFuncSetAttribute(rotate_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  rotate_rows_kernel<<<static_cast<unsigned>((rows + kRotRows - 1) / kRotRows), 256, smem,
+                       as_stream(stream)>>>(x, rows, d, x_row_stride, m, out, out_dtype,
+                                            out_row_stride);
+  return check_launch("ss_rotate_rows");
 }
 
 int ss_vq_scores_lut(const float* qdots, int nq, int nb, int k, const uint8_t* idx, int64_t t,

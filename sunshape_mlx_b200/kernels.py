@@ -106,6 +106,21 @@ def vq_assign(keys: torch.Tensor, centroids: torch.Tensor, *, perm: torch.Tensor
     return out_idx
 
 
+def rotate_rows(x: torch.Tensor, m: torch.Tensor, out_dtype=torch.float32) -> torch.Tensor:
+    """x (..., d) @ m (d, d) on the library's own kernel (fp32 fused
+    multiply-adds in index order); used for the rotations on the data path."""
+    L.require_cuda(x, m)
+    d = x.shape[-1]
+    xf = x.reshape(-1, d)
+    if xf.dtype != torch.float32 or xf.stride(-1) != 1:
+        xf = xf.float().contiguous()
+    mm = m.to(torch.float32).contiguous()
+    out = torch.empty((*x.shape[:-1], d), dtype=out_dtype, device=x.device)
+    L.call("ss_rotate_rows", L.ptr(xf), xf.shape[0], d, xf.stride(0), L.ptr(mm), L.ptr(out),
+           L.dtype_code(out_dtype), d, L.stream_ptr(x.device))
+    return out
+
+
 def set_assign_path(path: str = "auto") -> None:
     """Selects the assignment kernel process-wide: "auto", "simt" (CUDA cores)
     or "tensor" (tcgen05; raises for unsupported shapes). Results are identical."""

@@ -139,3 +139,24 @@ def test_query_centroid_dots_kernel(ss, cfg1_codec):
     # the gather over these tables reproduces the reference's cfg1 scores
     scores = want[:, np.arange(16)[None, :], g["indices"].astype(np.int64)].sum(-1)
     np.testing.assert_allclose(scores, g["scores"], atol=1e-4)
+
+
+@pytest.mark.parametrize("d,rows,odt", [(128, 1000, torch.float32), (64, 77, torch.float32),
+                                        (128, 129, torch.float16)])
+def test_rotate_rows_kernel(ss, d, rows, odt):
+    """The data-path rotations (rotated-mode keys, codec.py:273-293; the
+    TurboQuant value basis of the fp16 tail) on the library's own kernel,
+    against a float64 product."""
+    from sunshape_mlx_b200 import kernels as K
+
+    g = torch.Generator(device="cuda").manual_seed(d + rows)
+    x = torch.randn((rows, d), generator=g, device="cuda")
+    m = ss.generate_rotation_matrix(d, seed=3, device="cuda")
+    ss.reset_kernel_stats()
+    got = K.rotate_rows(x, m.T, odt)
+    assert ss.get_kernel_stats().get("ss_rotate_rows") == 1
+    want = x.double() @ m.T.double()
+    if odt == torch.float32:
+        assert float((got.double() - want).abs().max()) < 1e-5
+    else:
+        torch.testing.assert_close(got, want.half(), rtol=1e-3, atol=1e-3)
