@@ -578,76 +578,84 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(kn_empty + n % kKnRing);
         if (!heavy) {
-          // Pass 1 (ALU pipe): the row's minimum V, four independent chains,
-          // up to four 32-column chunks per TMEM wait.
+          // Pass 1 (ALU pipe): the minimum V of every 32-column chunk (one
+          // three-input min per two columns); chunk pairs per TMEM wait.
           const float inf = __int_as_float(0x7f800000);
-          float m0 = inf, m1 = inf, m2 = inf, m3 = inf;
-#pragma unroll 1
-          for (int ch = 0; ch < nch; ch += 4) {
-            const bool four = ch + 2 < nch;
-            uint32_t v0[32], v1[32], v2[32], v3[32];
-            tc_ld32(tbase + ch * 32, v0);
-            tc_ld32(tbase + (ch + 1) * 32, v1);
-            if (four) {
-              tc_ld32(tbase + (ch + 2) * 32, v2);
-              tc_ld32(tbase + (ch + 3) * 32, v3);
-            }
-            tc_wait_ld();
+          float cmin[8];
 #pragma unroll
-            for (int j = 0; j < 32; j += 2) {
-              m0 = fmin3(m0, __uint_as_float(v0[j]), __uint_as_float(v0[j + 1]));
-              m1 = fmin3(m1, __uint_as_float(v1[j]), __uint_as_float(v1[j + 1]));
-            }
-            if (four) {
+          for (int ch = 0; ch < 8; ch += 2) {
+            cmin[ch] = inf;
+            cmin[ch + 1] = inf;
+            if (ch < nch) {
+              uint32_t v0[32], v1[32];
+              tc_ld32(tbase + ch * 32, v0);
+              tc_ld32(tbase + (ch + 1) * 32, v1);  // nch is even
+              tc_wait_ld();
+              float m0 = inf, m1 = inf, m2 = inf, m3 = inf;
 #pragma unroll
-              for (int j = 0; j < 32; j += 2) {
-                m2 = fmin3(m2, __uint_as_float(v2[j]), __uint_as_float(v2[j + 1]));
-                m3 = fmin3(m3, __uint_as_float(v3[j]), __uint_as_float(v3[j + 1]));
+              for (int j = 0; j < 32; j += 4) {
+                m0 = fmin3(m0, __uint_as_float(v0[j]), __uint_as_float(v0[j + 1]));
+                m1 = fmin3(m1, __uint_as_float(v1[j]), __uint_as_float(v1[j + 1]));
+                m2 = fmin3(m2, __uint_as_float(v0[j + 2]), __uint_as_float(v0[j + 3]));
+                m3 = fmin3(m3, __uint_as_float(v1[j + 2]), __uint_as_float(v1[j + 3]));
               }
+              cmin[ch] = fminf(m0, m2);
+              cmin[ch + 1] = fminf(m1, m3);
             }
           }
-          const float s1 = fminf(fmin3(m0, m1, m2), m3);
-          // Pass 2 (FMA pipe): e = sat((s1 + T - V) * 4/T) is exactly 1 at
-          // the minimum and exactly 0 for every V >= s1 + T (up to rounding
-          // of 2^-8 T); cnt = sum e, pos = sum e * column. cnt == 1 means no
-          // other centroid within T of the minimum and rint(pos) is its column.
-          // Chunk pairs are double-buffered: the next pair's TMEM load is in
-          // flight while the current one is summed.
+          float s1 = inf;
+#pragma unroll
+          for (int q = 0; q < 8; q += 2) s1 = fmin3(s1, cmin[q], cmin[q + 1]);
+          // Pass 2: e = sat((s1 + T - V) * 4/T) is exactly 1 at the minimum and
+          // exactly 0 for every V >= s1 + T (up to rounding of 2^-8 T). The e of
+          // column j of every chunk accumulate into A[j] (packed fp32 pair adds),
+          // so a column costs one saturating FMA and half a packed add.
+          // cnt = sum A == 1 means no other centroid within T of the minimum;
+          // then A is one-hot at the winner's column within its chunk, and its
+          // chunk is the only one whose minimum equals s1.
           const float sn = kn + s_cmax[bl];
           const float tie = sn * kTieRel;
           const float big = 4.f / tie;
           const float thr_big = (s1 + tie) * big;
-          float cnt = 0.f, pos = 0.f;
-          auto sum_chunk = [&](const uint32_t (&v)[32], int ch) {
-            float ca = 0.f, pa = 0.f, cb = 0.f, pb = 0.f;
+          float ax[16], ay[16];
+#pragma unroll
+          for (int q = 0; q < 16; ++q) { ax[q] = 0.f; ay[q] = 0.f; }
+          auto sum_chunk = [&](const uint32_t (&v)[32]) {
 #pragma unroll
             for (int j = 0; j < 32; j += 2) {
-              const float e = fma_sat(__uint_as_float(v[j]), -big, thr_big);
-              ca += e;
-              pa = fmaf(e, (float)j, pa);
-              const float e2 = fma_sat(__uint_as_float(v[j + 1]), -big, thr_big);
-              cb += e2;
-              pb = fmaf(e2, (float)(j + 1), pb);
+              const float e0 = fma_sat(__uint_as_float(v[j]), -big, thr_big);
+              const float e1 = fma_sat(__uint_as_float(v[j + 1]), -big, thr_big);
+              add_f32x2(ax[j / 2], ay[j / 2], e0, e1);
             }
-            cnt += ca + cb;
-            pos += fmaf(ca + cb, (float)(ch * 32), pa + pb);
           };
           {
+            // chunk pairs double-buffered: the next TMEM load is in flight
+            // while the current chunk is summed
             uint32_t va[32], vb[32];
             tc_ld32(tbase, va);
             tc_wait_ld();
 #pragma unroll 1
             for (int ch = 0; ch < nch; ch += 2) {
               tc_ld32(tbase + (ch + 1) * 32, vb);  // nch is even
-              sum_chunk(va, ch);
+              sum_chunk(va);
               tc_wait_ld();
               if (ch + 2 < nch) tc_ld32(tbase + (ch + 2) * 32, va);
-              sum_chunk(vb, ch + 1);
+              sum_chunk(vb);
               tc_wait_ld();
             }
           }
+          float cnt = 0.f, pos = 0.f;
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            cnt += ax[q] + ay[q];
+            pos = fmaf(ax[q], (float)(2 * q), fmaf(ay[q], (float)(2 * q + 1), pos));
+          }
+          int wch = 0;
+#pragma unroll
+          for (int q = 7; q >= 0; --q)
+            if (cmin[q] == s1) wch = q;
           need = valid && !(cnt == 1.f && sn >= s_slo[bl] && sn <= s_shi[bl]);
-          idx = min(max((int)rintf(pos), 0), p.k - 1);
+          idx = min(max(wch * 32 + (int)rintf(pos), 0), p.k - 1);
         }
         tc_fence_before();
         __syncwarp();

@@ -237,6 +237,24 @@ __device__ __forceinline__ void add_f32x2(float& a, float& b, float x, float y) 
       : "f"(x), "f"(y));
 }
 
+// (a, b) *= s as one packed fp32 multiply (round to nearest).
+__device__ __forceinline__ void mul_f32x2(float& a, float& b, float s) {
+  asm("{\n .reg .b64 t, u;\n mov.b64 t, {%0, %1};\n mov.b64 u, {%2, %2};\n"
+      " mul.rn.f32x2 t, t, u;\n mov.b64 {%0, %1}, t;\n}"
+      : "+f"(a), "+f"(b)
+      : "f"(s));
+}
+
+// (a, b) = (a, b) * s + z with packed fp32 ops, a multiply then an add, as
+// the reference computes q * scale + zero in fp32 (two roundings).
+__device__ __forceinline__ void mul_add_f32x2(float& a, float& b, float s, float z) {
+  asm("{\n .reg .b64 t, u;\n mov.b64 t, {%0, %1};\n mov.b64 u, {%2, %2};\n"
+      " mul.rn.f32x2 t, t, u;\n mov.b64 u, {%3, %3};\n add.rn.f32x2 t, t, u;\n"
+      " mov.b64 {%0, %1}, t;\n}"
+      : "+f"(a), "+f"(b)
+      : "f"(s), "f"(z));
+}
+
 __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);

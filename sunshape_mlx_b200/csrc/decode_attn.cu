@@ -24,6 +24,7 @@
 // Quantized values are first decoded (levels * scale + zero) into an fp16
 // tile in the same swizzled layout and then take the same MMA path.
 #include <algorithm>
+#include <type_traits>
 #include <cfloat>
 #include <mutex>
 #include <string>
@@ -70,6 +71,8 @@ struct DecodeParams {
   int64_t vq_ps;
   int v_bits, v_group, v_words, v_groups;
   int v_gshift;              // log2(v_group) when a power of two, else -1
+  int vdec;                  // compressed value tiles: 0 fp16 (MMA straight from the
+                             // stage), 1 2-bit fast decoder, 2 block-VQ, 3 generic
   const void* vs;
   int vs_dt;
   int64_t vs_ps;
@@ -173,7 +176,7 @@ struct Misc {  // small shared-memory state
   float qc[8][128];     // scaled queries, codec space
   float mrow[8], lrow[8];
   float levels[16];
-  float2 lvpair[16];    // 2-bit values: levels of the two codes of each 4-bit nibble
+  alignas(128) float2 lvpair[16];  // 2-bit values: levels of the two codes of each nibble
   int heavy_pos[32];
   uint8_t is_heavy[128];
   int is_last;
@@ -545,6 +548,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
   for (int m = 0; m < 4; ++m) swz[m] = static_cast<uint32_t>(((2 * m + dsel) ^ mj) << 4);
   const int rows_valid = p.nrep * p.tq;
   const bool per_token_mask = p.causal || p.mask != nullptr;
+  const int vdec = p.vdec;
   // columns of every P slice that no row uses stay zero
   if constexpr (R < 4) {
     for (int e = lane; e < SL * 8; e += 32)
@@ -839,14 +843,22 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
           }
         }
       }
-      // masking: invalid tokens / rows -> -inf; causal; mask arrays
-      const int tg0 = (compressed ? t0 : static_cast<int>(p.tc) + t0) + tok0;
-      const int tg1 = tg0 + 32;
+      // masking: tokens past the end -> -inf; with causal or array masks also
+      // rows past the unit's last query row and the masks themselves (without
+      // them a missing row only gets scores nothing reads)
+      if (!per_token_mask) {
 #pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const bool rv = (rok >> r) & 1u;
-        bool ok0 = v0 && rv, ok1 = v1 && rv;
-        if (per_token_mask) {
+        for (int r = 0; r < R; ++r) {
+          if (!v0) s0[r] = -INFINITY;
+          if (!v1) s1[r] = -INFINITY;
+        }
+      } else {
+        const int tg0 = (compressed ? t0 : static_cast<int>(p.tc) + t0) + tok0;
+        const int tg1 = tg0 + 32;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const bool rv = (rok >> r) & 1u;
+          bool ok0 = v0 && rv, ok1 = v1 && rv;
           const int tqr = (rg * R + r) % p.tq;
           if (p.causal) {
             ok0 = ok0 && tg0 <= q_off + tqr;
@@ -863,9 +875,9 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
               if (p.mask_mode == 0) s1[r] += mv; else if (mv == 0.f) s1[r] = -FLT_MAX;
             }
           }
+          if (!ok0) s0[r] = -INFINITY;
+          if (!ok1) s1[r] = -INFINITY;
         }
-        if (!ok0) s0[r] = -INFINITY;
-        if (!ok1) s1[r] = -INFINITY;
       }
 
       // 2. online softmax over this warp's slice
@@ -875,15 +887,15 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
       for (int r = 0; r < R; ++r) {
         const float mx = warp_max_f32(TPL > 1 ? fmaxf(s0[r], s1[r]) : s0[r]);
         const float mn = fmaxf(m_w[r], mx);
-        float p0 = 0.f, p1 = 0.f;
+        float p0 = 0.f;
         if (mn == -INFINITY) {
           alpha[r] = 1.f;
         } else {
-          alpha[r] = fast_exp2((m_w[r] - mn) * kLog2e);
-          p0 = fast_exp2((s0[r] - mn) * kLog2e);
-          p1 = fast_exp2((s1[r] - mn) * kLog2e);
+          const float mnl = mn * kLog2e;
+          // exactly 1 when the running maximum did not move (no rescale then)
+          alpha[r] = m_w[r] == mn ? 1.f : fast_exp2(fmaf(m_w[r], kLog2e, -mnl));
+          p0 = fast_exp2(fmaf(s0[r], kLog2e, -mnl));
         }
-        (void)p1;
         const __half h0 = __float2half_rn(p0);
         ph0[r] = h0;
         pl0[r] = __float2half_rn(p0 - __half2float(h0));
@@ -932,7 +944,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
       __syncwarp();
 
       // 3. P.V: O^T[dims][rows] += V^T[dims][64 tokens] . P[64 tokens][rows]
-      if (p.vfmt == SS_V_F16) {
+      if (vdec == 0) {
         const uint32_t vb = smem_u32(st) + (slice * SL + kk_off) * 128;
 #pragma unroll
         for (int ks = 0; ks < SL / 16; ++ks) {
@@ -952,9 +964,14 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
         const uint32_t vb = smem_u32(vdq_w) + kk_off * 128;
         for (int ks = 0; ks < SL / 16; ++ks) {
           // decode 16 tokens of the slice into this warp's fp16 staging tile
-          if (compressed && p.vfmt == SS_V_QUANT && D == 128 && p.v_bits == 2 && p.v_group % 16 == 0) {
+          if (compressed && vdec == 1) {
             // 2-bit codes: lane = (token, half row); four 16-value words per
-            // lane in one 16-byte load, one nibble -> two levels per lookup
+            // lane in one 16-byte load. Per nibble (two codes): one shift, one
+            // three-input logic op forming the shared address of its level
+            // pair (the 128-byte-aligned pair table), one 8-byte load, one
+            // packed fp32 multiply (or multiply-add with the zero) and one
+            // fp16 pack -- the reference's fp32 level * scale (+ zero),
+            // rounded once to fp16.
             const uint8_t* sp = st + p.off_aux + TILE * p.v_words * 4;
             const float* zp = p.vz ? reinterpret_cast<const float*>(
                                          sp + TILE * p.v_groups * (p.vs_dt == SS_F32 ? 4 : 2))
@@ -963,28 +980,40 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
             const int tt = slice * SL + ks * 16 + tk;
             const uint4 wv = *reinterpret_cast<const uint4*>(st + p.off_aux + (tt * 8 + hw * 4) * 4);
             const uint32_t wrd[4] = {wv.x, wv.y, wv.z, wv.w};
+            const uint32_t lvb = smem_u32(&ms.lvpair[0]);
+            float sc[4], zr[4];
 #pragma unroll
             for (int wi = 0; wi < 4; ++wi) {
-              const int w = hw * 4 + wi;  // dims 16w .. 16w + 15
-              const int gi = p.v_gshift >= 0 ? (w * 16) >> p.v_gshift : (w * 16) / p.v_group;
-              const float s_ = p.vs_dt == SS_F32
-                                   ? reinterpret_cast<const float*>(sp)[tt * p.v_groups + gi]
-                                   : h2f(reinterpret_cast<const uint16_t*>(sp)[tt * p.v_groups + gi]);
-              const float z_ = zp ? zp[tt * p.v_groups + gi] : 0.f;
-              uint32_t h[8];
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const float2 lv = ms.lvpair[(wrd[wi] >> (4 * j)) & 15u];
-                float x0 = __fmul_rn(lv.x, s_), x1 = __fmul_rn(lv.y, s_);
-                if (zp) { x0 = __fadd_rn(x0, z_); x1 = __fadd_rn(x1, z_); }
-                h[j] = pack_h2(x0, x1);
-              }
-              *reinterpret_cast<uint4*>(vdq_w + vtile_addr(0, 16, tk, w * 16)) =
-                  make_uint4(h[0], h[1], h[2], h[3]);
-              *reinterpret_cast<uint4*>(vdq_w + vtile_addr(0, 16, tk, w * 16 + 8)) =
-                  make_uint4(h[4], h[5], h[6], h[7]);
+              const int gi = ((hw * 4 + wi) * 16) >> p.v_gshift;
+              sc[wi] = p.vs_dt == SS_F32 ? reinterpret_cast<const float*>(sp)[tt * p.v_groups + gi]
+                                         : h2f(reinterpret_cast<const uint16_t*>(sp)[tt * p.v_groups + gi]);
+              zr[wi] = zp ? zp[tt * p.v_groups + gi] : 0.f;
             }
-          } else if (compressed && p.vfmt == SS_V_VQ) {
+            auto decode = [&](auto with_zero) {
+#pragma unroll
+              for (int wi = 0; wi < 4; ++wi) {
+                const int w = hw * 4 + wi;  // dims 16w .. 16w + 15
+                uint32_t h[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  const uint32_t sh = j == 0 ? (wrd[wi] << 3) : (wrd[wi] >> (4 * j - 3));
+                  uint32_t a;
+                  asm("lop3.b32 %0, %1, 0x78, %2, 0xEA;" : "=r"(a) : "r"(sh), "r"(lvb));  // (sh & 0x78) | lvb
+                  float x0, x1;
+                  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(x0), "=f"(x1) : "r"(a));
+                  if constexpr (decltype(with_zero)::value) mul_add_f32x2(x0, x1, sc[wi], zr[wi]);
+                  else mul_f32x2(x0, x1, sc[wi]);
+                  h[j] = pack_h2(x0, x1);
+                }
+                *reinterpret_cast<uint4*>(vdq_w + vtile_addr(0, 16, tk, w * 16)) =
+                    make_uint4(h[0], h[1], h[2], h[3]);
+                *reinterpret_cast<uint4*>(vdq_w + vtile_addr(0, 16, tk, w * 16 + 8)) =
+                    make_uint4(h[4], h[5], h[6], h[7]);
+              }
+            };
+            if (zp) decode(std::true_type{});
+            else decode(std::false_type{});
+          } else if (compressed && vdec == 2) {
             // block-VQ values: lane = (token, half row); one index byte per
             // block, one table row of v_bd fp16 per block
             const int tk = lane >> 1, hw = lane & 1;
@@ -1583,6 +1612,9 @@ int run_decode(const ss_decode_args* a, float* part_out, void* stream,
   p.idx = a->idx; p.idx_ps = a->idx_pair_stride;
   p.kheavy = a->kheavy; p.kh_ps = a->kheavy_pair_stride;
   p.vfmt = a->vfmt; p.v_ps = a->v_pair_stride; p.vq = a->vq; p.vq_ps = a->vq_pair_stride;
+  p.vdec = a->vfmt == SS_V_F16 ? 0
+           : a->vfmt == SS_V_VQ ? 2
+           : (a->d == 128 && a->v_bits == 2 && a->v_group % 16 == 0) ? 1 : 3;
   p.v_gshift = -1;
   for (int sh = 0; sh < 12; ++sh)
     if (a->v_group == (1 << sh)) p.v_gshift = sh;
