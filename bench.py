@@ -532,8 +532,8 @@ def run_config(args, world, rank, local):
                 pr.run()
         launches = 2 * layers
     elif world > 1 and args.config == 5:
-        def step():
-            splitkv.splitkv_sdpa(q, cache, scale)
+        sk = splitkv.PreparedSplitKV(q, cache, scale)
+        step = sk.run
         launches = 3  # table + decode (partials) + merge; plus the NCCL all-gather
     else:
         prep = PreparedDecode(q, cache, scale)
@@ -576,7 +576,7 @@ def run_config(args, world, rank, local):
     ms = float(ms_t)
     phases = None
     if world > 1 and args.config == 5:
-        phases = _splitkv_phases(q, cache, scale, args.steps, device)
+        phases = _splitkv_phases(sk, args.steps, device)
     if rank != 0:
         return None
     peak, peak_kind = _peaks()
@@ -611,25 +611,23 @@ def run_config(args, world, rank, local):
     return line
 
 
-def _splitkv_phases(q, cache, scale, steps, device):
+def _splitkv_phases(sk, steps, device):
     """Per-phase device time of the split-KV step (this rank's fused decode
     partials, the NCCL all-gather, the log-sum-exp merge), CUDA events around
     each phase, averaged over `steps` steps, max over ranks."""
     import torch
     import torch.distributed as dist
-    from sunshape_mlx_b200 import splitkv
-    from sunshape_mlx_b200.attention import decode_partials
 
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
     dist.barrier()
     torch.cuda.synchronize()
     for i in range(steps):
         ev[i][0].record()
-        part = decode_partials(q, cache, scale)
+        sk.run_partials()
         ev[i][1].record()
-        parts = splitkv.all_gather_partials(part)
+        sk.gather()
         ev[i][2].record()
-        splitkv.merge_partials(parts, q.shape, q.dtype)
+        sk.merge()
         ev[i][3].record()
     torch.cuda.synchronize()
     t = torch.tensor([[e[k].elapsed_time(e[k + 1]) for k in range(3)] for e in ev],
@@ -945,6 +943,13 @@ def run_reference(args):
     return line
 
 
+_OUT = sys.stdout
+
+
+def _emit(line_json: str, flush: bool = True) -> None:
+    print(line_json, file=_OUT, flush=flush)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -968,23 +973,28 @@ def main():
                     help="build the workload, run warmup+steps decode launches, exit "
                          "(short command for ncu captures)")
     args = ap.parse_args()
+    # stdout carries exactly the one JSON line: anything else a library prints
+    # there (NCCL's version banner, for one) is sent to stderr
+    global _OUT
+    _OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         if rank == 0:
-            print(json.dumps(run_reference(args)), flush=True)
+            _emit(json.dumps(run_reference(args)))
         return
     import torch
     import torch.distributed as dist
 
     if args.encode:
-        print(json.dumps(run_encode(args)), flush=True)
+        _emit(json.dumps(run_encode(args)))
         return
     if args.assign:
         line = run_assign(args)
         if line is not None:
-            print(json.dumps(line), flush=True)
+            _emit(json.dumps(line))
         return
     if world > 1:
         torch.cuda.set_device(local)
@@ -992,13 +1002,13 @@ def main():
     if args.config == 4 and args.model:
         line = run_model(args, rank, local)
         if line is not None:
-            print(json.dumps(line), flush=True)
+            _emit(json.dumps(line))
         return
     if args.config != 2:
         try:
             line = run_config(args, world, rank, local)
             if line is not None:
-                print(json.dumps(line), flush=True)
+                _emit(json.dumps(line))
         finally:
             if world > 1:
                 dist.destroy_process_group()
@@ -1018,7 +1028,7 @@ def main():
     try:
         line = run_ours(args, world, rank, local)
         if line is not None:
-            print(json.dumps(line), flush=True)
+            _emit(json.dumps(line))
     finally:
         if world > 1:
             dist.destroy_process_group()

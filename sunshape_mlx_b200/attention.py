@@ -295,10 +295,14 @@ class PreparedDecode:
     ``out`` in place."""
 
     def __init__(self, q: torch.Tensor, cache, scale: float, out: torch.Tensor | None = None,
-                 max_ctas: int = 0, wait_limit_ns: int = 0, _test_skip_tile: int = -1):
+                 max_ctas: int = 0, wait_limit_ns: int = 0, _test_skip_tile: int = -1,
+                 part_out: torch.Tensor | None = None):
         codec = cache.codec
         self.q = q
-        self.out = out if out is not None else torch.empty_like(q)
+        # part_out (B*Hq*Tq, D+2) f32: write this shard's (o, m, l) rows instead
+        # of the output (the split-KV step, ss_decode_attn_partial)
+        self.part_out = part_out
+        self.out = None if part_out is not None else (out if out is not None else torch.empty_like(q))
         spec = cache.attention_spec()
         spec["max_ctas"] = max_ctas
         perm = codec.permutation if codec._is_perm() else None
@@ -320,6 +324,7 @@ class PreparedDecode:
         self._a.test_skip_tile = int(_test_skip_tile) + 1 if _test_skip_tile >= 0 else 0
         self._lib = lib
         self._ref = C.byref(self._a)
+        self._part_ptr = C.c_void_p(part_out.data_ptr()) if part_out is not None else None
         self.device = q.device
 
     def run(self, stream=None, check: bool = False) -> torch.Tensor:
@@ -330,11 +335,14 @@ class PreparedDecode:
         if w is not None and w.value:
             L.poll_device_errors()
         st = C.c_void_p(stream if stream is not None else torch.cuda.current_stream(self.device).cuda_stream)
-        rc = self._lib.ss_decode_attn(self._ref, st)
+        if self.part_out is None:
+            rc = self._lib.ss_decode_attn(self._ref, st)
+        else:
+            rc = self._lib.ss_decode_attn_partial(self._ref, self._part_ptr, st)
         if rc:
             L.check("ss_decode_attn", rc)
         if check:
             if stream is not None:
                 torch.cuda.synchronize(self.device)
             L.check_device_errors(self.device)
-        return self.out
+        return self.out if self.part_out is None else self.part_out

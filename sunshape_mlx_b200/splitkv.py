@@ -16,7 +16,8 @@ import torch.distributed as dist
 
 from . import _lib as L
 
-__all__ = ["shard_range", "all_gather_partials", "merge_partials", "splitkv_sdpa"]
+__all__ = ["shard_range", "all_gather_partials", "merge_partials", "splitkv_sdpa",
+           "PreparedSplitKV"]
 
 
 def shard_range(n_tokens: int, rank: int, world: int) -> tuple[int, int]:
@@ -59,3 +60,51 @@ def splitkv_sdpa(queries: torch.Tensor, shard_cache, scale: float, group=None) -
     if spec.get("v_rot") is not None:
         v_rot = spec["v_rot"].contiguous()
     return merge_partials(parts, queries.shape, queries.dtype, v_rot)
+
+
+class PreparedSplitKV:
+    """The split-KV decode step with everything built once (the argument
+    block of this shard's fused decode, the gather and output buffers): each
+    ``run()`` is one C call for this shard's (o, m, l) rows, one all-gather
+    into a kept buffer and one C call for the log-sum-exp merge, so the host
+    issues a step in microseconds. The shard cache must not be reallocated
+    between calls; queries are read from ``q`` in place."""
+
+    def __init__(self, q: torch.Tensor, shard_cache, scale: float, group=None):
+        import ctypes as C
+
+        from .attention import PreparedDecode
+
+        B, Hq, Tq, D = q.shape
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.part = torch.empty((B * Hq * Tq, D + 2), dtype=torch.float32, device=q.device)
+        self.decode = PreparedDecode(q, shard_cache, scale, part_out=self.part)
+        self.parts = torch.empty((self.world, *self.part.shape), dtype=torch.float32,
+                                 device=q.device)
+        self.out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+        vr = shard_cache.attention_spec().get("v_rot")
+        self.v_rot = vr.contiguous() if vr is not None else None
+        self._lib = L.load()
+        self._merge_args = (C.c_void_p(self.parts.data_ptr()), self.world, self.part.shape[0], D,
+                            L.ptr(self.v_rot), C.c_void_p(self.out.data_ptr()),
+                            L.dtype_code(q.dtype), D)
+        self.device = q.device
+
+    def run_partials(self) -> torch.Tensor:
+        return self.decode.run()
+
+    def gather(self) -> None:
+        if dist.get_backend(self.group) == "nccl":
+            dist.all_gather_into_tensor(self.parts, self.part, group=self.group)
+        else:
+            self.parts.copy_(all_gather_partials(self.part, self.group))
+
+    def merge(self) -> torch.Tensor:
+        L.check("ss_lse_merge", self._lib.ss_lse_merge(*self._merge_args, L.stream_ptr(self.device)))
+        return self.out
+
+    def run(self) -> torch.Tensor:
+        self.run_partials()
+        self.gather()
+        return self.merge()
