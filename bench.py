@@ -258,9 +258,20 @@ def run_ours(args, world, rank, local):
         kd = din[nq:nq + nkv].view(B, HKV, 1, D)
         vd = din[nq + nkv:].view(B, HKV, 1, D)
 
+        # The query copy runs on a side stream, overlapping the new token's
+        # copy and cache append on the main stream; the attention waits for it.
+        side = torch.cuda.Stream(device)
+        q_ready = torch.cuda.Event()
+        nq_b = nq  # query elements first in the staging buffer
+
         def e2e_step():
-            din.copy_(hin, non_blocking=True)
+            side.wait_stream(st)  # the previous step's attention has read the query
+            with torch.cuda.stream(side):
+                din[:nq_b].copy_(hin[:nq_b], non_blocking=True)
+                q_ready.record(side)
+            din[nq_b:].copy_(hin[nq_b:], non_blocking=True)
             cache.append(kd, vd)
+            st.wait_event(q_ready)
             out = ss.sunshape_sdpa(qd, cache, scale)
             oh.copy_(out, non_blocking=True)
             cache.trim(1)

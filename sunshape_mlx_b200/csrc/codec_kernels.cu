@@ -222,6 +222,15 @@ __global__ void __launch_bounds__(kAssignThreads) vq_assign_small_kernel(AssignP
                   : 0.f;
   }
   const bool heavy = p.heavy && p.heavy[b];
+  // the block's centroids, staged once with coalesced loads: the loop below
+  // then reads them from shared memory instead of one dependent global
+  // load per centroid
+  __shared__ __align__(16) float s_c[256 * 16];
+  const float* cb = p.cents + (size_t)b * p.k * BD;
+  if (!heavy) {
+    for (int e = tid; e < p.k * BD; e += kAssignThreads) s_c[e] = __ldg(cb + e);
+  }
+  __syncthreads();
   if (heavy) {
     if (warp == 0 && valid) {
       if (p.out_heavy) {
@@ -240,13 +249,12 @@ __global__ void __launch_bounds__(kAssignThreads) vq_assign_small_kernel(AssignP
     }
     return;
   }
-  const float* cb = p.cents + (size_t)b * p.k * BD;
   const int per = (p.k + 15) / 16;
   const int c0 = warp * per, c1 = min(p.k, c0 + per);
   float best = __int_as_float(0x7f800000);
   int bi = 0x7fffffff;
   for (int c = c0; c < c1; ++c) {
-    const float* cc = cb + (size_t)c * BD;
+    const float* cc = s_c + c * BD;
     const float dd = p.dist_mode == 0 ? dist_direct<BD>(kk, cc) : dist_expanded<BD>(kk, cc);
     if (c == 0) s_d0[lane] = dd;
     if (dd < best) { best = dd; bi = c; }
