@@ -12,8 +12,9 @@ collective on the data path).
   value : device throughput of the fused kernel with everything resident,
           queries/s summed over ranks (max-over-ranks step time).
   e2e   : the same metric through the public API per step: pinned-host->device
-          copy of the step's query and new K/V token, cache.append (quantize +
-          store), sunshape_sdpa, device->host copy of the output.
+          copy of the step's query (side stream) and new K/V token, cache.append
+          (deferred: the next sunshape_sdpa's table launch quantizes and stores
+          the token), sunshape_sdpa, device->host copy of the output.
 
 python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -293,7 +294,7 @@ def run_ours(args, world, rank, local):
         e2e = {"value": world * B * HQ / (ems / 1e3), "unit": "queries/s",
                "h2d_bytes_per_step": qh.numel() * 2 + kh.numel() * 2 + vh.numel() * 2,
                "d2h_bytes_per_step": oh.numel() * 2, "ms_per_step": ems,
-               "gpu_launches_per_step": 3}  # assign (append) + table + decode
+               "gpu_launches_per_step": 2}  # table kernel (with the fused append) + decode
 
     if rank != 0:
         return None

@@ -300,6 +300,21 @@ typedef struct ss_decode_args {
    * flattened tile t - 1 while still expecting their bytes, so the waits on
    * that tile run out (exercises the timeout path without a GPU fault). */
   int64_t test_skip_tile;
+  /* Optional cache append fused into this call (NULL app_keys: none). The
+   * newest app_rows tokens of every (batch, kv-head) pair -- positions
+   * tc - app_rows .. tc - 1, already counted in tc -- are not yet in the
+   * streams: this call quantizes app_keys into idx (heavy blocks into
+   * kheavy) and stores app_values as fp16 rows of v, exactly as
+   * ss_cache_append would, before any tile holding them is read (the write
+   * half of update_and_fetch, cache.py:156-205, and the attention in one
+   * step). Keys/values are (pair, token, d) with the given strides in
+   * elements, dtype app_dtype. Supported for fp16 values, no fp16 tail,
+   * permutation/identity codecs with 4- or 8-dim blocks and at most 4096
+   * appended rows in all; otherwise SS_ERR_UNSUPPORTED (nothing written). */
+  const void* app_keys; const void* app_values; int app_dtype;
+  int64_t app_key_pair_stride, app_key_row_stride;
+  int64_t app_value_pair_stride, app_value_row_stride;
+  int64_t app_rows;
 } ss_decode_args;
 
 size_t ss_decode_workspace_size(const ss_decode_args* a);

@@ -72,6 +72,10 @@ class DecodeArgs(C.Structure):
         ("workspace", vp), ("workspace_bytes", C.c_size_t),
         ("max_ctas", i32),
         ("wait_limit_ns", i64), ("test_skip_tile", i64),
+        ("app_keys", vp), ("app_values", vp), ("app_dtype", i32),
+        ("app_key_pair_stride", i64), ("app_key_row_stride", i64),
+        ("app_value_pair_stride", i64), ("app_value_row_stride", i64),
+        ("app_rows", i64),
     ]
 
 

@@ -226,8 +226,9 @@ def _sdpa_simple_fast(q: torch.Tensor, cache, scale: float) -> torch.Tensor:
            codec.centroids.data_ptr(), codec.permutation.data_ptr(), codec.use_rotation,
            None if vcod is None else (vcod.centroids.data_ptr(), vcod.centroids._version))
     memo = cache._sdpa_memo
+    pend = getattr(cache, "_pending", None)
     if memo is None or memo[0] != key:
-        spec = cache.attention_spec()
+        spec = cache.attention_spec(flush=False) if pend is not None else cache.attention_spec()
         perm = codec.permutation if codec._is_perm() else None
         rot_k = codec.rotation.contiguous() if codec.use_rotation else None
         n_heavy = codec.n_heavy_blocks if spec.get("kheavy") is not None else 0
@@ -258,7 +259,26 @@ def _sdpa_simple_fast(q: torch.Tensor, cache, scale: float) -> torch.Tensor:
         ws_by_tiles[tiles] = ws
     a.workspace = ws.data_ptr()
     a.workspace_bytes = ws.numel()
-    rc = lib.ss_decode_attn(ref, C.c_void_p(sp))
+    if pend is not None:
+        # the deferred append of this step is written by this launch's table
+        # kernel (ss_decode_args.app_*); fall back to a separate append when
+        # the fused form does not apply
+        k, v, o, T = pend
+        a.app_keys, a.app_values, a.app_dtype = k.data_ptr(), v.data_ptr(), L.dtype_code(k.dtype)
+        a.app_key_pair_stride, a.app_key_row_stride = k.stride(1), k.stride(2)
+        a.app_value_pair_stride, a.app_value_row_stride = v.stride(1), v.stride(2)
+        a.app_rows = T if o + T == cache.offset and k.dtype == v.dtype else 0
+        if a.app_rows == 0:
+            a.app_keys = None
+            cache._flush_pending()
+        rc = lib.ss_decode_attn(ref, C.c_void_p(sp))
+        a.app_keys, a.app_values, a.app_rows = None, None, 0
+        if rc == 2 and cache._pending is not None:  # unsupported fused form
+            cache._flush_pending()
+            rc = lib.ss_decode_attn(ref, C.c_void_p(sp))
+        cache._pending = None
+    else:
+        rc = lib.ss_decode_attn(ref, C.c_void_p(sp))
     if rc:
         L.check("ss_decode_attn", rc)
     codec.last_score_backend = "cuda_fused"

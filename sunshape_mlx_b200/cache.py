@@ -162,6 +162,11 @@ class SunShapeKVCache:
         self._assign_memo = None
         self._sdpa_memo = None
         self.eager_fetch = False  # True: update_and_fetch materializes keys (reference behaviour)
+        # A decode step's append is handed to the next sunshape_sdpa call, which
+        # quantizes and stores the tokens in its own table launch
+        # (ss_decode_args.app_*); any other reader writes them first.
+        self.defer_append = True
+        self._pending = None      # (keys, values, offset, tokens) not yet written
 
     # ------------------------------------------------------------ storage
     def _ensure_capacity(self, B: int, new_tokens: int) -> None:
@@ -198,8 +203,17 @@ class SunShapeKVCache:
             raise AssertionError(f"Expected head_dim {self.head_dim}, got {D}")
         if T == 0:
             return
+        self._flush_pending()
         self._ensure_capacity(B, T)
         o = self.offset
+        codec = self.codec
+        if (self.defer_append and B * H * T <= 4096 and not codec.use_rotation
+                and codec.block_dim in (4, 8) and k.stride(3) == 1 and v.shape == k.shape
+                and v.stride(3) == 1 and k.stride(0) == H * k.stride(1)
+                and v.stride(0) == H * v.stride(1)):
+            self._pending = (k, v, o, T)
+            self.offset += T
+            return
         if not self._append_fast(k, v, o):
             _quantize_keys_into(self.codec, k, self._key_indices[:, :, o:o + T],
                                 None if self._key_heavy is None else self._key_heavy[:, :, o:o + T])
@@ -254,6 +268,18 @@ class SunShapeKVCache:
             K.L.check("ss_cache_append", rc)
         return True
 
+    def _flush_pending(self) -> None:
+        """Writes a deferred append now (one ss_cache_append launch)."""
+        pend = self._pending
+        if pend is None:
+            return
+        self._pending = None
+        k, v, o, T = pend
+        if not self._append_fast(k, v, o):
+            _quantize_keys_into(self.codec, k, self._key_indices[:, :, o:o + T],
+                                None if self._key_heavy is None else self._key_heavy[:, :, o:o + T])
+            self._values.narrow(2, o, T).copy_(v)
+
     def update_and_fetch(self, keys, values):
         """cache.py:156-205: append, then return (keys, values) as stored.
         The keys are a DeferredTensor (dequantized on first use only: the
@@ -267,14 +293,19 @@ class SunShapeKVCache:
             return self.keys
         idx, kh, t = self._key_indices, self._key_heavy, self.offset
         codec = self.codec
+
+        def fetch():
+            self._flush_pending()
+            return _dequantize_keys(codec, idx[:, :, :t], None if kh is None else kh[:, :, :t])
         return DeferredTensor(
-            lambda: _dequantize_keys(codec, idx[:, :, :t], None if kh is None else kh[:, :, :t]),
+            fetch,
             (self._batch, self.n_kv_heads, t, self.head_dim), torch.float32, self.device)
 
     # ------------------------------------------------------------ views
     @property
     def keys(self) -> torch.Tensor:
         """Dequantized keys (B, H, T, D) float32 (cache.py:211-240)."""
+        self._flush_pending()
         if self._key_indices is None or self.offset == 0:
             return torch.zeros((1, self.n_kv_heads, 0, self.head_dim), dtype=torch.float32,
                                device=self.device)
@@ -283,6 +314,7 @@ class SunShapeKVCache:
 
     @property
     def values(self) -> torch.Tensor:
+        self._flush_pending()
         if self._values is None or self.offset == 0:
             return torch.zeros((1, self.n_kv_heads, 0, self.head_dim), dtype=self.dtype,
                                device=self.device)
@@ -290,6 +322,7 @@ class SunShapeKVCache:
 
     @property
     def key_indices(self) -> torch.Tensor:
+        self._flush_pending()
         if self._key_indices is None or self.offset == 0:
             return torch.zeros((1, self.n_kv_heads, 0, self.n_blocks), dtype=torch.uint8,
                                device=self.device)
@@ -300,7 +333,11 @@ class SunShapeKVCache:
         return (self.key_indices, self.values)
 
     # ------------------------------------------------------------ fused-attention view
-    def attention_spec(self) -> dict:
+    def attention_spec(self, flush: bool = True) -> dict:
+        """Streams and token count for the fused kernel. flush=False leaves a
+        deferred append pending (the caller's launch writes it)."""
+        if flush:
+            self._flush_pending()
         cap = self._capacity
         spec = dict(tc=self.offset, cap=cap, idx=self._key_indices, v=self._values)
         if self._key_heavy is not None:
@@ -333,6 +370,7 @@ class SunShapeKVCache:
         return True
 
     def trim(self, n: int) -> None:
+        self._flush_pending()
         self.offset = max(0, self.offset - n)
 
     def empty(self) -> bool:
@@ -876,6 +914,8 @@ def _codec_from_state(st: dict, device) -> SunShapeBlockCodec:
 
 
 def _cache_state(cache) -> dict:
+    if hasattr(cache, "_flush_pending"):
+        cache._flush_pending()
     fields = {}
     for name, val in vars(cache).items():
         if name.endswith("_memo") or name in ("codec", "value_codec", "_value_codec_impl", "device"):

@@ -40,16 +40,54 @@ struct AssignParams {
 };
 
 // Value rows of a cache append: rows [r0, r0 + n) of the (group, row) space,
-// d elements each, converted to f16 (the cache's value dtype).
+// d elements each, converted to f16 (the cache's value dtype). Loads are
+// issued in batches of 8 before their stores (the source and destination may
+// alias as far as the compiler knows, which would otherwise serialize every
+// element on a memory round trip); fp16 rows with 16-byte aligned strides
+// move as 16-byte chunks.
 __device__ __forceinline__ void copy_value_rows(const AssignParams& p, int64_t r0, int n,
                                                 int tid, int nthr) {
   const int64_t n_rows = p.n_groups * p.rpg;
-  for (int e = tid; e < n * p.d; e += nthr) {
-    const int rr = e / p.d, j = e - rr * p.d;
-    const int64_t r = r0 + rr;
-    if (r >= n_rows) continue;
-    const int64_t g = r / p.rpg, t = r - g * p.rpg;
-    p.vdst[g * p.vdgs + t * p.vdrs + j] = f2h(load_as_f32(p.vsrc, p.vdt, g * p.vgs + t * p.vrs + j));
+  const bool vec = p.vdt == SS_F16 && p.d % 8 == 0 &&
+                   (reinterpret_cast<uintptr_t>(p.vsrc) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(p.vdst) & 15) == 0 && (p.vgs * 2) % 16 == 0 &&
+                   (p.vrs * 2) % 16 == 0 && (p.vdgs * 2) % 16 == 0 && (p.vdrs * 2) % 16 == 0;
+  if (vec) {
+    const int cpr = p.d / 8;  // 16-byte chunks per row
+    for (int e = tid; e < n * cpr; e += nthr) {
+      const int rr = e / cpr, ch = e - rr * cpr;
+      const int64_t r = r0 + rr;
+      if (r >= n_rows) continue;
+      const int64_t g = r / p.rpg, t = r - g * p.rpg;
+      const uint4 v = *reinterpret_cast<const uint4*>(
+          static_cast<const uint16_t*>(p.vsrc) + g * p.vgs + t * p.vrs + ch * 8);
+      *reinterpret_cast<uint4*>(p.vdst + g * p.vdgs + t * p.vdrs + ch * 8) = v;
+    }
+    return;
+  }
+  for (int e0 = tid; e0 < n * p.d; e0 += 8 * nthr) {
+    float x[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int e = e0 + u * nthr;
+      const int rr = e / p.d, j = e - rr * p.d;
+      const int64_t r = r0 + rr;
+      x[u] = 0.f;
+      if (e < n * p.d && r < n_rows) {
+        const int64_t g = r / p.rpg, t = r - g * p.rpg;
+        x[u] = load_as_f32(p.vsrc, p.vdt, g * p.vgs + t * p.vrs + j);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int e = e0 + u * nthr;
+      const int rr = e / p.d, j = e - rr * p.d;
+      const int64_t r = r0 + rr;
+      if (e < n * p.d && r < n_rows) {
+        const int64_t g = r / p.rpg, t = r - g * p.rpg;
+        p.vdst[g * p.vdgs + t * p.vdrs + j] = f2h(x[u]);
+      }
+    }
   }
 }
 

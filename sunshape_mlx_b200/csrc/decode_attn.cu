@@ -30,6 +30,7 @@
 #include <string>
 
 #include "common.cuh"
+#include "vq_math.cuh"
 
 namespace ss {
 namespace {
@@ -104,6 +105,14 @@ struct DecodeParams {
   int* sink;                // process error sink (host word) or null
   uint64_t wait_ns;         // bound of every barrier wait
   int64_t skip_tile;        // test hook: tile whose copies are never issued (-1: none)
+  // fused cache append (app_rows > 0): the newest app_rows tokens of every pair
+  const void* app_k;
+  const void* app_v;
+  int app_dt;
+  int64_t app_kps, app_krs, app_vps, app_vrs, app_rows;
+  int app_groups;           // 32-row append CTAs per key block
+  int lut_groups;           // table CTAs per key block (grid.y below the append CTAs)
+  uint16_t* v_w;            // fp16 value stream (append writes)
   int* counters;
   float* slots;
   float* lut_g;             // per-unit query x centroid tables [unit][nb][k][R]
@@ -217,6 +226,176 @@ __device__ __forceinline__ void unit_codec_rows(const DecodeParams& p, const flo
       v = qo[r][p.perm ? p.perm[j] : j];
     }
     qc[r][j] = v;
+  }
+}
+
+// Table kernel for permutation / identity codecs with 4- or 8-dim blocks:
+// grid (block b, group of kLutUnits units); thread c holds centroid row c of
+// block b in registers and writes entry (b, c) of the tables of all the
+// group's units, so every CTA reads one block's centroids (k * BD floats)
+// once instead of every unit reading all of them. Same arithmetic as
+// lut_kernel: query rows dtype(q * scale) (attention.py:208), picked through
+// the permutation, fused multiply-adds in dim order, zero for pass-through
+// blocks.
+constexpr int kLutUnits = 4;
+// Fused cache append, one CTA per (key block b, 32 appended rows): lane =
+// row, warp w scans centroids [w * per, (w + 1) * per) in order with a
+// strict '<' and the warps' winners are combined in warp order -- the first
+// index whose distance is below every earlier one, as the reference's
+// sequential loop and ss_cache_append (a NaN distance at index 0 keeps 0).
+// Distances in NumPy's order (dist_direct). Heavy blocks store the fp16
+// key values and index 0. CTAs of block 0 also store the value rows.
+template <int BD>
+__device__ __forceinline__ void append_rows(const DecodeParams& p, int b, int64_t a) {
+  __shared__ __align__(16) float s_c[256 * BD];
+  __shared__ float s_best[8][32];
+  __shared__ int s_bi[8][32];
+  __shared__ float s_d0[32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t n_rows = (int64_t)p.b * p.hkv * p.app_rows;
+  const int64_t r = a * 32 + lane;
+  const bool valid = r < n_rows;
+  int64_t pair = 0, tt = 0;
+  if (valid) { pair = r / p.app_rows; tt = r - pair * p.app_rows; }
+  const int64_t pos = p.tc - p.app_rows + tt;
+  float kk[BD];
+#pragma unroll
+  for (int j = 0; j < BD; ++j) {
+    const int col = b * BD + j;
+    kk[j] = valid ? load_as_f32(p.app_k, p.app_dt, pair * p.app_kps + tt * p.app_krs +
+                                                       (p.perm ? __ldg(p.perm + col) : col))
+                  : 0.f;
+  }
+  if (b == 0) {
+    // the value rows of these 32 tokens, as fp16, in 8-element chunks whose
+    // loads all issue before their stores (source and destination may alias
+    // as far as the compiler knows)
+    const int cpr = p.d / 8;
+    for (int e = tid; e < 32 * cpr; e += 256) {
+      const int rr = e / cpr, j0 = (e - rr * cpr) * 8;
+      const int64_t ro = a * 32 + rr;
+      if (ro >= n_rows) continue;
+      const int64_t pr = ro / p.app_rows, tr = ro - pr * p.app_rows;
+      const int64_t src = pr * p.app_vps + tr * p.app_vrs + j0;
+      float x[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) x[j] = load_as_f32(p.app_v, p.app_dt, src + j);
+      uint4 h;
+      h.x = pack_h2(x[0], x[1]); h.y = pack_h2(x[2], x[3]);
+      h.z = pack_h2(x[4], x[5]); h.w = pack_h2(x[6], x[7]);
+      *reinterpret_cast<uint4*>(p.v_w + pr * p.v_ps + (p.tc - p.app_rows + tr) * p.d + j0) = h;
+    }
+  }
+  const bool heavy = p.n_heavy > 0 && p.heavy && p.heavy[b];
+  if (heavy) {
+    if (warp == 0 && valid) {
+      int hpos = 0;
+      for (int bb = 0; bb < b; ++bb) hpos += p.heavy[bb] ? 1 : 0;
+      uint16_t* dst = const_cast<uint16_t*>(p.kheavy) + pair * p.kh_ps +
+                      pos * (p.n_heavy * p.bd) + hpos * BD;
+#pragma unroll
+      for (int j = 0; j < BD; ++j) dst[j] = f2h(kk[j]);
+      const_cast<uint8_t*>(p.idx)[pair * p.idx_ps + pos * p.nb + b] = 0;
+    }
+    return;
+  }
+  const float* cb = p.cents + (size_t)b * p.k * BD;
+  for (int e = tid; e < p.k * BD; e += 256) s_c[e] = __ldg(cb + e);
+  __syncthreads();
+  const int per = (p.k + 7) / 8;
+  const int c0 = warp * per, c1 = min(p.k, c0 + per);
+  float best = __int_as_float(0x7f800000);
+  int bi = 0x7fffffff;
+  for (int c = c0; c < c1; ++c) {
+    const float dd = dist_direct<BD>(kk, s_c + c * BD);
+    if (c == 0) s_d0[lane] = dd;
+    if (dd < best) { best = dd; bi = c; }
+  }
+  s_best[warp][lane] = best;
+  s_bi[warp][lane] = bi;
+  __syncthreads();
+  if (warp == 0 && valid) {
+    float bv = s_best[0][lane];
+    int bx = s_bi[0][lane];
+    for (int w = 1; w < 8; ++w)
+      if (s_best[w][lane] < bv) { bv = s_best[w][lane]; bx = s_bi[w][lane]; }
+    const float d0 = s_d0[lane];
+    const int idx = (d0 != d0 || bx == 0x7fffffff) ? 0 : bx;
+    const_cast<uint8_t*>(p.idx)[pair * p.idx_ps + pos * p.nb + b] = static_cast<uint8_t>(idx);
+  }
+}
+
+template <int R, int BD>
+__global__ void __launch_bounds__(256) lut_block_kernel(const __grid_constant__ DecodeParams p) {
+  __shared__ __align__(16) float qs[kLutUnits][R][BD];
+  const int tid = threadIdx.x;
+  const int b = blockIdx.x;
+  if ((int)blockIdx.y >= p.lut_groups) {  // fused cache append
+    grid_launch_dependents();
+    append_rows<BD>(p, b, (int64_t)blockIdx.y - p.lut_groups);
+    return;
+  }
+  const int64_t u0 = (int64_t)blockIdx.y * kLutUnits;
+  grid_launch_dependents();  // let the decode grid start streaming now
+  const float sc = round_to(p.scale, p.qdt);
+  const int rows_valid = p.nrep * p.tq;
+  for (int e = tid; e < kLutUnits * R * BD; e += 256) {
+    const int ui = e / (R * BD), rem = e - ui * (R * BD), r = rem / BD, j = rem - r * BD;
+    const int64_t u = u0 + ui;
+    float v = 0.f;
+    if (u < p.n_units) {
+      const int64_t pair = u / p.n_rg;
+      const int rg = static_cast<int>(u - pair * p.n_rg);
+      const int bb = static_cast<int>(pair / p.hkv), hh = static_cast<int>(pair % p.hkv);
+      const int rr = rg * R + r;
+      if (rr < rows_valid) {
+        const int rep = rr / p.tq, tqi = rr - rep * p.tq;
+        const int qh = hh * p.nrep + rep;
+        const int col = p.perm ? __ldg(p.perm + b * BD + j) : b * BD + j;
+        v = round_to(load_as_f32(p.q, p.qdt, bb * p.q_sb + qh * p.q_sh + tqi * p.q_st + col) * sc,
+                     p.qdt);
+      }
+    }
+    qs[ui][r][j] = v;
+  }
+  const int c = tid;
+  const bool zero = p.n_heavy > 0 && p.heavy && p.heavy[b];
+  float cv[BD];
+#pragma unroll
+  for (int j = 0; j < BD; j += 4) {
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (c < p.k) v = __ldg(reinterpret_cast<const float4*>(p.cents + ((size_t)b * p.k + c) * BD + j));
+    cv[j] = v.x; cv[j + 1] = v.y; cv[j + 2] = v.z; cv[j + 3] = v.w;
+  }
+  __syncthreads();
+  if (c >= p.k) return;
+#pragma unroll 2
+  for (int ui = 0; ui < kLutUnits; ++ui) {
+    const int64_t u = u0 + ui;
+    if (u >= p.n_units) break;
+    float o[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      float qv[BD];
+#pragma unroll
+      for (int j = 0; j < BD; j += 4) {
+        const float4 q4 = *reinterpret_cast<const float4*>(&qs[ui][r][j]);
+        qv[j] = q4.x; qv[j + 1] = q4.y; qv[j + 2] = q4.z; qv[j + 3] = q4.w;
+      }
+      float acc = 0.f;
+#pragma unroll
+      for (int j = 0; j < BD; ++j) acc = fmaf(zero ? 0.f : qv[j], cv[j], acc);
+      o[r] = acc;
+    }
+    float* dst = p.lut_g + (size_t)u * (p.lut_unit_bytes / 4) + ((size_t)b * p.k + c) * R;
+    if constexpr (R % 4 == 0) {
+#pragma unroll
+      for (int r = 0; r < R; r += 4)
+        *reinterpret_cast<float4*>(dst + r) = make_float4(o[r], o[r + 1], o[r + 2], o[r + 3]);
+    } else {
+#pragma unroll
+      for (int r = 0; r < R; ++r) dst[r] = o[r];
+    }
   }
 }
 
@@ -434,6 +613,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
       int64_t pair = u / p.n_rg;
       int rgc = static_cast<int>(u - pair * p.n_rg);
       int s = 0, ph = 0;  // stage of tile `it` and its use count parity
+      bool dep_done = false;
       for (int64_t tau = t_begin; tau < t_end; ++tau, ++it) {
         if (tau != t_begin && ++lt == p.tpu) {
           lt = 0;
@@ -451,6 +631,12 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
         uint8_t* st = smem + (size_t)s * p.stage_bytes;
         if (lt < p.n_ct) {
           const int64_t t0 = (int64_t)lt * TILE;
+          // tokens appended by this step's table kernel (the primary of this
+          // programmatic dependent launch): wait for it before reading them
+          if (p.app_rows > 0 && !dep_done && t0 + TILE > p.tc - p.app_rows) {
+            grid_dependency_wait();
+            dep_done = true;
+          }
           uint32_t bytes = TILE * p.nb;
           if (p.vfmt == SS_V_F16) bytes += TILE * D * 2;
           else bytes += p.v_tile_bytes;
@@ -1495,9 +1681,17 @@ int launch_decode(const DecodeParams& p, const CUtensorMap& mv, const CUtensorMa
     cudaFuncSetAttribute(lut_kernel<R, 0>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     carveout_set = true;
   }
-  if (p.bd == 8) lut_kernel<R, 8><<<lgrid, kLutThreads, 0, st>>>(p);
-  else if (p.bd == 4) lut_kernel<R, 4><<<lgrid, kLutThreads, 0, st>>>(p);
-  else lut_kernel<R, 0><<<lgrid, kLutThreads, 0, st>>>(p);
+  if (p.rot_k == nullptr && (p.bd == 8 || p.bd == 4) && p.k <= 256) {
+    const dim3 bgrid(static_cast<unsigned>(p.nb), static_cast<unsigned>(p.lut_groups + p.app_groups));
+    if (p.bd == 8) lut_block_kernel<R, 8><<<bgrid, 256, 0, st>>>(p);
+    else lut_block_kernel<R, 4><<<bgrid, 256, 0, st>>>(p);
+  } else if (p.bd == 8) {
+    lut_kernel<R, 8><<<lgrid, kLutThreads, 0, st>>>(p);
+  } else if (p.bd == 4) {
+    lut_kernel<R, 4><<<lgrid, kLutThreads, 0, st>>>(p);
+  } else {
+    lut_kernel<R, 0><<<lgrid, kLutThreads, 0, st>>>(p);
+  }
   int rc = check_launch("ss_decode_attn (tables)");
   if (rc != SS_OK) return rc;
   const bool nb16 = p.nb == 16 && p.k == 256;
@@ -1640,6 +1834,27 @@ int run_decode(const ss_decode_args* a, float* part_out, void* stream,
   p.slots = reinterpret_cast<float*>(ws + pl.off_slots);
   p.lut_g = reinterpret_cast<float*>(ws + pl.off_lut_g);
   p.lut_unit_bytes = static_cast<uint32_t>(pl.lut_unit_bytes);
+  p.lut_groups = static_cast<int>((pl.n_units + kLutUnits - 1) / kLutUnits);
+  p.app_rows = 0;
+  p.app_groups = 0;
+  if (a->app_keys) {
+    const int64_t rows = (int64_t)a->b * a->hkv * a->app_rows;
+    SS_REQUIRE(a->app_values && a->app_rows >= 1 && a->app_rows <= a->tc,
+               "ss_decode_attn: bad fused append (app_values / app_rows)");
+    SS_REQUIRE(a->app_dtype >= SS_F32 && a->app_dtype <= SS_BF16, "ss_decode_attn: bad app_dtype");
+    if (!(a->vfmt == SS_V_F16 && a->ttail == 0 && a->rot_k == nullptr &&
+          (a->bd == 4 || a->bd == 8) && rows <= 4096))
+      return fail(SS_ERR_UNSUPPORTED, "ss_decode_attn: fused append needs fp16 values, no fp16 "
+                                      "tail, a permutation codec with 4- or 8-dim blocks and "
+                                      "<= 4096 appended rows");
+    p.app_k = a->app_keys; p.app_v = a->app_values; p.app_dt = a->app_dtype;
+    p.app_kps = a->app_key_pair_stride; p.app_krs = a->app_key_row_stride;
+    p.app_vps = a->app_value_pair_stride; p.app_vrs = a->app_value_row_stride;
+    p.app_rows = a->app_rows;
+    p.app_groups = static_cast<int>((rows + 31) / 32);
+    p.v_w = const_cast<uint16_t*>(reinterpret_cast<const uint16_t*>(a->v));
+    count_dispatch("ss_cache_append (fused into ss_decode_attn)");
+  }
   p.stage_bytes = pl.stage_bytes; p.off_idx = pl.off_idx; p.off_aux = pl.off_aux;
   p.off_vdq = pl.off_vdq; p.off_lut = pl.off_lut; p.off_p = pl.off_p; p.off_misc = pl.off_misc;
   p.off_plo = pl.off_plo;

@@ -49,7 +49,8 @@ def test_decode_args_layout_matches_header():
     from sunshape_mlx_b200 import _lib as L
 
     fields = ["q", "scale", "centroids", "n_heavy", "tc", "vfmt", "v_levels", "v_rot", "ttail",
-              "causal", "mask_mode", "out", "workspace", "max_ctas"]
+              "causal", "mask_mode", "out", "workspace", "max_ctas", "wait_limit_ns",
+              "test_skip_tile", "app_keys", "app_dtype", "app_value_row_stride", "app_rows"]
     prog = "#include <cstdio>\n#include <cstddef>\n#include \"%s\"\nint main(){printf(\"%%zu\", sizeof(ss_decode_args));%s}\n" % (
         HEADER, "".join(f'printf(" %zu", offsetof(ss_decode_args, {f}));' for f in fields))
     with tempfile.TemporaryDirectory() as d:

@@ -112,7 +112,10 @@ def test_kernel_stats_and_backend_breadcrumbs(ss, cfg1_codec):
     ss.sunshape_sdpa(q, cache, 0.088)
     st = ss.get_kernel_stats()
     assert st.get("ss_decode_attn", 0) >= 1
-    assert st.get("ss_cache_append", 0) + st.get("ss_vq_assign", 0) >= 1
+    # the append is deferred into the decode launch (or, when that does not
+    # apply, a separate ss_cache_append / ss_vq_assign)
+    assert (st.get("ss_cache_append", 0) + st.get("ss_vq_assign", 0)
+            + st.get("ss_cache_append (fused into ss_decode_attn)", 0)) >= 1
     assert cfg1_codec.last_score_backend == "cuda_fused"
     qz = cfg1_codec.quantize(torch.tensor(kk[0, 0], device="cuda"))
     cfg1_codec.attention_scores(torch.randn(4, 128, device="cuda"), qz)
@@ -160,3 +163,54 @@ def test_rotate_rows_kernel(ss, d, rows, odt):
         assert float((got.double() - want).abs().max()) < 1e-5
     else:
         torch.testing.assert_close(got, want.half(), rtol=1e-3, atol=1e-3)
+
+
+@pytest.mark.parametrize("kind,T,dt", [("perm", 1, torch.float16), ("perm", 3, torch.bfloat16),
+                                       ("mixed", 1, torch.float32), ("bd4", 1, torch.float16)])
+def test_deferred_append_fused_into_decode(ss, kind, T, dt):
+    """A decode step's append (update_and_fetch) handed to the next
+    sunshape_sdpa, whose table launch quantizes and stores the new tokens:
+    the cache streams and the output equal those of a separate append
+    (ss_cache_append) bit for bit, over several steps; any other reader
+    (keys, trim, a second append) writes a pending append first."""
+    rng = np.random.default_rng(7)
+    kc = rng.standard_normal((2048, 128)).astype(np.float32)
+    qc = I.heavy_tailed_queries(1024, 128, seed=3)
+    if kind == "mixed":
+        codec = ss.SunShapeBlockCodec(head_dim=128, mode="profileperm_mixed_precision", n_heavy=4)
+    else:
+        codec = ss.SunShapeBlockCodec(head_dim=128, block_dim=4 if kind == "bd4" else 8)
+    codec.fit(qc, kc, kmeans_iters=2, seed=0)
+    caches = [ss.create_kv_cache(codec, n_kv_heads=4) for _ in range(2)]
+    caches[1].defer_append = False
+    g = torch.Generator(device="cuda").manual_seed(11)
+    pre_k = torch.randn((2, 4, 300, 128), generator=g, device="cuda").to(dt)
+    pre_v = torch.randn((2, 4, 300, 128), generator=g, device="cuda").to(dt)
+    for c in caches:
+        c.append(pre_k, pre_v)
+    for step in range(4):
+        k = torch.randn((2, 4, T, 128), generator=g, device="cuda").to(dt)
+        v = torch.randn((2, 4, T, 128), generator=g, device="cuda").to(dt)
+        q = torch.randn((2, 16, 1, 128), generator=g, device="cuda").half()
+        outs = []
+        for c in caches:
+            c.update_and_fetch(k, v)
+            outs.append(ss.sunshape_sdpa(q, c, 1 / math.sqrt(128)))
+        assert caches[0]._pending is None
+        torch.testing.assert_close(outs[0], outs[1], rtol=0, atol=0)
+        assert torch.equal(caches[0].key_indices, caches[1].key_indices)
+        assert torch.equal(caches[0].values, caches[1].values)
+        if kind == "mixed":
+            assert torch.equal(caches[0]._key_heavy[:, :, :caches[0].offset],
+                               caches[1]._key_heavy[:, :, :caches[1].offset])
+    # readers other than the fused decode write the pending tokens first
+    k = torch.randn((2, 4, T, 128), generator=g, device="cuda").to(dt)
+    for c in caches:
+        c.append(k, k)
+    assert caches[0]._pending is not None
+    torch.testing.assert_close(caches[0].keys, caches[1].keys, rtol=0, atol=0)
+    assert caches[0]._pending is None
+    for c in caches:
+        c.append(k, k)
+        c.trim(1)
+    assert torch.equal(caches[0].key_indices, caches[1].key_indices)

@@ -220,6 +220,7 @@ def test_cache_append_matches_assign_and_values(ss, B, T, heavy, kdt):
     codec = ss.SunShapeBlockCodec(head_dim=128, mode=mode, **({"n_heavy": 4} if heavy else {}))
     codec.fit(qc, kc, kmeans_iters=2, seed=0)
     cache = ss.create_kv_cache(codec, n_kv_heads=2)
+    cache.defer_append = False  # this test is about ss_cache_append itself
     k0 = torch.tensor(rng.standard_normal((B, 2, 37, 128)), device="cuda").half()
     cache.append(k0, k0 * 2)
     k = torch.tensor(rng.standard_normal((B, 2, T, 128)), device="cuda").to(kdt)
