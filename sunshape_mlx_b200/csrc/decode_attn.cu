@@ -735,6 +735,12 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
   const int rows_valid = p.nrep * p.tq;
   const bool per_token_mask = p.causal || p.mask != nullptr;
   const int vdec = p.vdec;
+  // vdec 4: this lane's byte offsets (from the stage base, first 16-token
+  // step) of its four packed value words and of its two fp16 group scales
+  const uint32_t q4_word_off =
+      p.off_aux + (uint32_t)(((warp % (TILE / SL)) * SL + (lane >> 1)) * 8 + (lane & 1) * 4) * 4;
+  const uint32_t q4_scale_off = p.off_aux + TILE * 8 * 4 +
+      (uint32_t)(((warp % (TILE / SL)) * SL + (lane >> 1)) * 4 + (lane & 1) * 2) * 2;
   // columns of every P slice that no row uses stay zero
   if constexpr (R < 4) {
     for (int e = lane; e < SL * 8; e += 32)
@@ -1150,7 +1156,42 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
         const uint32_t vb = smem_u32(vdq_w) + kk_off * 128;
         for (int ks = 0; ks < SL / 16; ++ks) {
           // decode 16 tokens of the slice into this warp's fp16 staging tile
-          if (compressed && vdec == 1) {
+          if (compressed && vdec == 4) {
+            // The 2-bit format with fp16 scales per 32 channels and no zeros
+            // (the long TurboQuant-value workload): the same decoder with the
+            // lane's word and scale offsets fixed for the launch and its two
+            // scales in one 4-byte load.
+            const int tk = lane >> 1, hw = lane & 1;
+            const uint32_t sb = smem_u32(st);
+            uint32_t w0, w1, w2, w3, s2;
+            asm("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                : "=r"(w0), "=r"(w1), "=r"(w2), "=r"(w3) : "r"(sb + q4_word_off + ks * 512));
+            asm("ld.shared.u32 %0, [%1];" : "=r"(s2) : "r"(sb + q4_scale_off + ks * 128));
+            const uint32_t wrd[4] = {w0, w1, w2, w3};
+            const float sca = __half2float(__ushort_as_half(static_cast<unsigned short>(s2 & 0xffffu)));
+            const float scb = __half2float(__ushort_as_half(static_cast<unsigned short>(s2 >> 16)));
+            const uint32_t lvb = smem_u32(&ms.lvpair[0]);
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi) {
+              const int w = hw * 4 + wi;  // dims 16w .. 16w + 15
+              const float scw = wi < 2 ? sca : scb;
+              uint32_t h[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const uint32_t sh = j == 0 ? (wrd[wi] << 3) : (wrd[wi] >> (4 * j - 3));
+                uint32_t a;
+                asm("lop3.b32 %0, %1, 0x78, %2, 0xEA;" : "=r"(a) : "r"(sh), "r"(lvb));
+                float x0, x1;
+                asm("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(x0), "=f"(x1) : "r"(a));
+                mul_f32x2(x0, x1, scw);
+                h[j] = pack_h2(x0, x1);
+              }
+              *reinterpret_cast<uint4*>(vdq_w + vtile_addr(0, 16, tk, w * 16)) =
+                  make_uint4(h[0], h[1], h[2], h[3]);
+              *reinterpret_cast<uint4*>(vdq_w + vtile_addr(0, 16, tk, w * 16 + 8)) =
+                  make_uint4(h[4], h[5], h[6], h[7]);
+            }
+          } else if (compressed && vdec == 1) {
             // 2-bit codes: lane = (token, half row); four 16-value words per
             // lane in one 16-byte load. Per nibble (two codes): one shift, one
             // three-input logic op forming the shared address of its level
@@ -1186,7 +1227,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
                   uint32_t a;
                   asm("lop3.b32 %0, %1, 0x78, %2, 0xEA;" : "=r"(a) : "r"(sh), "r"(lvb));  // (sh & 0x78) | lvb
                   float x0, x1;
-                  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(x0), "=f"(x1) : "r"(a));
+                  asm("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(x0), "=f"(x1) : "r"(a));
                   if constexpr (decltype(with_zero)::value) mul_add_f32x2(x0, x1, sc[wi], zr[wi]);
                   else mul_f32x2(x0, x1, sc[wi]);
                   h[j] = pack_h2(x0, x1);
@@ -1808,6 +1849,8 @@ int run_decode(const ss_decode_args* a, float* part_out, void* stream,
   p.vfmt = a->vfmt; p.v_ps = a->v_pair_stride; p.vq = a->vq; p.vq_ps = a->vq_pair_stride;
   p.vdec = a->vfmt == SS_V_F16 ? 0
            : a->vfmt == SS_V_VQ ? 2
+           : (a->d == 128 && a->v_bits == 2 && a->v_group == 32 && a->v_scale_dtype == SS_F16 &&
+              !a->v_zeros) ? 4
            : (a->d == 128 && a->v_bits == 2 && a->v_group % 16 == 0) ? 1 : 3;
   p.v_gshift = -1;
   for (int sh = 0; sh < 12; ++sh)
