@@ -917,7 +917,34 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
       if (compressed) {
         const uint8_t* ir0 = st + p.off_idx + tok0 * p.nb;
         const uint8_t* ir1 = st + p.off_idx + tok1 * p.nb;
-        if (NBC > 0 || (p.nb & 3) == 0) {
+        if constexpr (NBC > 0 && R % 4 == 0 && TPL == 1) {
+          // 16 blocks: each (block, centroid) row of the table is R floats;
+          // R/2 packed fp32 pair accumulators take the 16-byte loads as two
+          // 64-bit halves (no register shuffling between the load and the
+          // packed add); block order as in the generic loop below
+          uint64_t acc2[R / 2];
+#pragma unroll
+          for (int i = 0; i < R / 2; ++i) acc2[i] = 0ull;
+          const uint32_t lbase = smem_u32(lut);
+#pragma unroll
+          for (int w = 0; w < NBC / 4; ++w) {
+            const uint32_t c0w = v0 ? reinterpret_cast<const uint32_t*>(ir0)[w] : 0u;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t a = lbase + ((4 * w + j) * 256u * R + __byte_perm(c0w, 0u, 0x4440u + j) * R) * 4u;
+#pragma unroll
+              for (int r4 = 0; r4 < R; r4 += 4) {
+                uint64_t x, y;
+                asm("ld.shared.v2.b64 {%0, %1}, [%2];" : "=l"(x), "=l"(y) : "r"(a + r4 * 4));
+                asm("add.rn.f32x2 %0, %0, %1;" : "+l"(acc2[r4 / 2]) : "l"(x));
+                asm("add.rn.f32x2 %0, %0, %1;" : "+l"(acc2[r4 / 2 + 1]) : "l"(y));
+              }
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < R / 2; ++i)
+            asm("mov.b64 {%0, %1}, %2;" : "=f"(s0[2 * i]), "=f"(s0[2 * i + 1]) : "l"(acc2[i]));
+        } else if (NBC > 0 || (p.nb & 3) == 0) {
           const int nbw = NBC > 0 ? NBC / 4 : (p.nb >> 2);
           // floats per block of the table (compile-time for 16 blocks x 256 centroids)
           const uint32_t kstride = NBC > 0 ? 256u * R : static_cast<uint32_t>(p.k) * R;
@@ -1171,19 +1198,24 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
             const float sca = __half2float(__ushort_as_half(static_cast<unsigned short>(s2 & 0xffffu)));
             const float scb = __half2float(__ushort_as_half(static_cast<unsigned short>(s2 >> 16)));
             const uint32_t lvb = smem_u32(&ms.lvpair[0]);
+            uint64_t sa2, sb2;  // each scale twice, as a packed pair
+            asm("mov.b64 %0, {%1, %1};" : "=l"(sa2) : "f"(sca));
+            asm("mov.b64 %0, {%1, %1};" : "=l"(sb2) : "f"(scb));
 #pragma unroll
             for (int wi = 0; wi < 4; ++wi) {
               const int w = hw * 4 + wi;  // dims 16w .. 16w + 15
-              const float scw = wi < 2 ? sca : scb;
+              const uint64_t s2 = wi < 2 ? sa2 : sb2;
               uint32_t h[8];
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
                 const uint32_t sh = j == 0 ? (wrd[wi] << 3) : (wrd[wi] >> (4 * j - 3));
                 uint32_t a;
                 asm("lop3.b32 %0, %1, 0x78, %2, 0xEA;" : "=r"(a) : "r"(sh), "r"(lvb));
+                uint64_t x;
+                asm("ld.shared.b64 %0, [%1];" : "=l"(x) : "r"(a));
+                asm("mul.rn.f32x2 %0, %0, %1;" : "+l"(x) : "l"(s2));
                 float x0, x1;
-                asm("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(x0), "=f"(x1) : "r"(a));
-                mul_f32x2(x0, x1, scw);
+                asm("mov.b64 {%0, %1}, %2;" : "=f"(x0), "=f"(x1) : "l"(x));
                 h[j] = pack_h2(x0, x1);
               }
               *reinterpret_cast<uint4*>(vdq_w + vtile_addr(0, 16, tk, w * 16)) =
