@@ -171,7 +171,8 @@ def _prepare_mask(mask, tq: int, tkv: int, device) -> tuple[torch.Tensor | None,
     return m.to(torch.float32).contiguous(), 0, False
 
 
-def sunshape_sdpa(queries, cache, scale: float, mask=None, *, check: bool = False) -> torch.Tensor:
+def sunshape_sdpa(queries, cache, scale: float, mask=None, *, check: bool = False,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
     """Scaled dot-product attention over a SunShape cache (attention.py:166-352).
 
     queries (B, n_q_heads, T_q, D) in the model basis; the cache's key indices,
@@ -181,30 +182,45 @@ def sunshape_sdpa(queries, cache, scale: float, mask=None, *, check: bool = Fals
     Every call first raises SunShapeCudaError (timeout) if an earlier launch
     gave up on a bounded device-side wait (its output was invalid); with
     ``check=True`` the call also synchronizes and checks its own launch.
+
+    ``out`` (optional, queries' shape and dtype) receives the result: a CUDA
+    tensor, or a page-locked host tensor that the kernel writes in place
+    (the result then needs no separate device-to-host copy; it is complete
+    once the stream reaches this point).
     """
     L.poll_device_errors()
-    out = _sdpa(queries, cache, scale, mask)
+    res = _sdpa(queries, cache, scale, mask, out)
     if check:
-        L.check_device_errors(out.device)
-    return out
+        L.check_device_errors(cache.device)
+    return res
 
 
-def _sdpa(queries, cache, scale: float, mask=None) -> torch.Tensor:
+def _sdpa(queries, cache, scale: float, mask=None, out_user=None) -> torch.Tensor:
     q = K.cuda_tensor(queries, device=cache.device)
+    if out_user is not None:
+        if tuple(out_user.shape) != tuple(q.shape) or out_user.dtype != q.dtype:
+            raise ValueError("out must have the queries' shape and dtype")
+        if not (out_user.is_cuda or out_user.is_pinned()) or out_user.stride(-1) != 1:
+            raise ValueError("out must be a CUDA or page-locked host tensor, contiguous in head_dim")
+        if not out_user.is_cuda and not q.is_contiguous():
+            raise ValueError("a host out needs contiguous queries")
     B, Hq, Tq, D = q.shape
     if Hq % cache.n_kv_heads:
         raise ValueError("n_q_heads must be a multiple of n_kv_heads")
     tkv = cache.offset
     if tkv == 0:
+        if out_user is not None:
+            out_user.zero_()
+            return out_user
         return torch.zeros_like(q)
     if mask is None and (isinstance(cache, SunShapeKVCache) or
                          (isinstance(cache, HybridSunShapeKVCache) and cache._buffer_offset == 0)):
-        return _sdpa_simple_fast(q, cache, scale)
+        return _sdpa_simple_fast(q, cache, scale, out_user)
     codec = cache.codec
     spec = cache.attention_spec()
     m, mode, causal = _prepare_mask(mask, Tq, tkv, q.device)
     spec["mask_mode"] = mode
-    out = torch.empty_like(q)
+    out = out_user if out_user is not None else torch.empty_like(q)
     perm = codec.permutation if codec._is_perm() else None
     rot_k = codec.rotation.contiguous() if codec.use_rotation else None
     n_heavy = codec.n_heavy_blocks if spec.get("kheavy") is not None else 0
@@ -214,7 +230,7 @@ def _sdpa(queries, cache, scale: float, mask=None) -> torch.Tensor:
     return out
 
 
-def _sdpa_simple_fast(q: torch.Tensor, cache, scale: float) -> torch.Tensor:
+def _sdpa_simple_fast(q: torch.Tensor, cache, scale: float, out_user=None) -> torch.Tensor:
     """sunshape_sdpa without a mask for the simple cache, or a hybrid cache
     whose fp16 tail is empty (then every token is compressed): the argument block
     is kept on the cache and rebuilt only when the storage is reallocated or
@@ -240,7 +256,9 @@ def _sdpa_simple_fast(q: torch.Tensor, cache, scale: float) -> torch.Tensor:
         memo = (key, a, keep, lib, C.byref(a), {})
         cache._sdpa_memo = memo
     _, a, _, lib, ref, ws_by_tiles = memo
-    out = torch.empty_like(q)
+    if out_user is not None and out_user.stride() != q.stride():
+        raise ValueError("out must have the queries' strides")
+    out = out_user if out_user is not None else torch.empty_like(q)
     a.q = q.data_ptr()
     a.out = out.data_ptr()
     a.tc = cache.offset

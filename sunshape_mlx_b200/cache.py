@@ -192,10 +192,15 @@ class SunShapeKVCache:
 
     def append(self, keys, values) -> None:
         """Quantize and store new tokens without materialising anything
-        (the write half of update_and_fetch)."""
+        (the write half of update_and_fetch). Page-locked host tensors
+        (``pin_memory()``) of a deferred decode-step append are not copied:
+        the kernel that writes them reads them from host memory directly."""
         L.poll_device_errors()
-        k = K.cuda_tensor(keys, device=self.device)
-        v = K.cuda_tensor(values, device=self.device)
+        if _pinned(keys) and _pinned(values) and self.defer_append:
+            k, v = keys, values
+        else:
+            k = K.cuda_tensor(keys, device=self.device)
+            v = K.cuda_tensor(values, device=self.device)
         B, H, T, D = k.shape
         if H != self.n_kv_heads:
             raise AssertionError(f"Expected {self.n_kv_heads} kv heads, got {H}")
@@ -214,6 +219,8 @@ class SunShapeKVCache:
             self._pending = (k, v, o, T)
             self.offset += T
             return
+        if not k.is_cuda:
+            k, v = K.cuda_tensor(k, device=self.device), K.cuda_tensor(v, device=self.device)
         if not self._append_fast(k, v, o):
             _quantize_keys_into(self.codec, k, self._key_indices[:, :, o:o + T],
                                 None if self._key_heavy is None else self._key_heavy[:, :, o:o + T])
@@ -276,6 +283,8 @@ class SunShapeKVCache:
         self._pending = None
         k, v, o, T = pend
         if not self._append_fast(k, v, o):
+            if not k.is_cuda:
+                k, v = K.cuda_tensor(k, device=self.device), K.cuda_tensor(v, device=self.device)
             _quantize_keys_into(self.codec, k, self._key_indices[:, :, o:o + T],
                                 None if self._key_heavy is None else self._key_heavy[:, :, o:o + T])
             self._values.narrow(2, o, T).copy_(v)
@@ -383,6 +392,11 @@ class SunShapeKVCache:
         return (f"SunShapeKVCache(offset={self.offset}, head_dim={self.head_dim}, "
                 f"n_blocks={self.n_blocks}, n_centroids={self.n_centroids}, "
                 f"compression={self.compression_ratio:.1f}x)")
+
+
+def _pinned(x) -> bool:
+    """A page-locked host tensor (readable by the GPU in place)."""
+    return isinstance(x, torch.Tensor) and not x.is_cuda and x.is_pinned()
 
 
 def _quantize_keys_into(codec: SunShapeBlockCodec, keys: torch.Tensor, idx_out: torch.Tensor,

@@ -214,3 +214,35 @@ def test_deferred_append_fused_into_decode(ss, kind, T, dt):
         c.append(k, k)
         c.trim(1)
     assert torch.equal(caches[0].key_indices, caches[1].key_indices)
+
+
+def test_pinned_host_append_and_output(ss, cfg1_codec):
+    """Page-locked host tensors for a decode step: the new K/V token is read
+    by the append kernel from host memory in place, and the attention output
+    is written straight into a host tensor; results equal the device path."""
+    caches = [ss.create_kv_cache(cfg1_codec, n_kv_heads=2) for _ in range(2)]
+    kk, vv = I.kv_stream(51, 2, 2, 500, 128)
+    for c in caches:
+        c.append(kk, vv)
+    g = torch.Generator().manual_seed(5)
+    for step in range(3):
+        k = torch.randn((2, 2, 1, 128), generator=g).half().pin_memory()
+        v = torch.randn((2, 2, 1, 128), generator=g).half().pin_memory()
+        q = torch.randn((2, 8, 1, 128), generator=g).half()
+        qd = q.cuda()
+        host_out = torch.empty((2, 8, 1, 128), dtype=torch.float16).pin_memory()
+        caches[0].append(k, v)                      # stays on the host until the launch
+        assert not caches[0]._pending[0].is_cuda
+        r0 = ss.sunshape_sdpa(qd, caches[0], 0.088, out=host_out)
+        caches[1].append(k.cuda(), v.cuda())
+        r1 = ss.sunshape_sdpa(qd, caches[1], 0.088)
+        torch.cuda.synchronize()
+        assert r0 is host_out
+        torch.testing.assert_close(host_out, r1.cpu(), rtol=0, atol=0)
+        assert torch.equal(caches[0].key_indices, caches[1].key_indices)
+        assert torch.equal(caches[0].values, caches[1].values)
+    # a pending host append written by another reader (flush through ss_cache_append)
+    k = torch.randn((2, 2, 1, 128), generator=g).half().pin_memory()
+    caches[0].append(k, k)
+    caches[1].append(k.cuda(), k.cuda())
+    assert torch.equal(caches[0].key_indices, caches[1].key_indices)
