@@ -2,8 +2,8 @@
 
     python -m sunshape_mlx_b200.build          # or: python sunshape_mlx_b200/build.py
 
-nvcc cross-compiles for sm_100a without a GPU. Objects are rebuilt only when
-a source or header is newer than the library.
+nvcc cross-compiles for sm_100a without a GPU. An object is rebuilt only when
+its source or a header is newer than it; stale objects compile in parallel.
 """
 
 from __future__ import annotations
@@ -48,14 +48,24 @@ def build(force: bool = False, verbose: bool = False) -> str:
     nvcc = _nvcc()
     objdir = os.path.join(HERE, "_build")
     os.makedirs(objdir, exist_ok=True)
-    objs = []
+    headers = glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(INCLUDE, "*.h"))
+    objs, cmds = [], []
     for src in sources():
         obj = os.path.join(objdir, os.path.basename(src)[:-3] + ".o")
-        cmd = [nvcc, *ARCH, *FLAGS, "-I", INCLUDE, "-c", src, "-o", obj]
+        objs.append(obj)
+        fresh = os.path.exists(obj) and all(
+            os.path.getmtime(d) <= os.path.getmtime(obj) for d in [src, *headers])
+        if force or not fresh:
+            cmds.append([nvcc, *ARCH, *FLAGS, "-I", INCLUDE, "-c", src, "-o", obj])
+    # objects compile independently: run them side by side
+    procs = []
+    for cmd in cmds:
         if verbose:
             print(" ".join(cmd), flush=True)
-        subprocess.run(cmd, check=True)
-        objs.append(obj)
+        procs.append(subprocess.Popen(cmd))
+    failed = [c for c, pr in zip(cmds, procs) if pr.wait() != 0]
+    if failed:
+        raise subprocess.CalledProcessError(1, failed[0])
     tmp = LIB + ".tmp"
     cmd = [nvcc, *ARCH, "-shared", "-o", tmp, *objs, "-lcudart"]
     if verbose:

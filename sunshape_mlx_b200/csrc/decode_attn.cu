@@ -560,7 +560,7 @@ __global__ void __launch_bounds__(kLutThreads) lut_kernel(const __grid_constant_
   }
 }
 
-template <int R, int D, int NBC, int CW, bool HV>
+template <int R, int D, int NBC, int CW, bool HV, int LEAN = 0>
 __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
     const __grid_constant__ DecodeParams p, const __grid_constant__ CUtensorMap map_v,
     const __grid_constant__ CUtensorMap map_vt) {
@@ -733,8 +733,8 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
 #pragma unroll
   for (int m = 0; m < 4; ++m) swz[m] = static_cast<uint32_t>(((2 * m + dsel) ^ mj) << 4);
   const int rows_valid = p.nrep * p.tq;
-  const bool per_token_mask = p.causal || p.mask != nullptr;
-  const int vdec = p.vdec;
+  const bool per_token_mask = LEAN ? false : (p.causal || p.mask != nullptr);
+  const int vdec = LEAN == 1 ? 0 : LEAN == 2 ? 4 : p.vdec;
   // vdec 4: this lane's byte offsets (from the stage base, first 16-token
   // step) of its four packed value words and of its two fp16 group scales
   const uint32_t q4_word_off =
@@ -761,7 +761,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
   const uint2* hqs = reinterpret_cast<const uint2*>(&ms.qc[0][0]);
   bool heavy_mma = false;
 
-  if (p.vfmt == SS_V_VQ) {
+  if (!LEAN && p.vfmt == SS_V_VQ) {
     // value centroids, once per CTA: [v_nb][256][v_bd] fp16 with entries
     // c >= v_k zeroed, so any stored index byte reads a finite row (the
     // unit loop's first barrier publishes the table)
@@ -815,7 +815,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
         bulk_g2s(reinterpret_cast<uint8_t*>(lut) + off, src + off,
                  bytes - off < 16384u ? bytes - off : 16384u, &lut_bar);
     }
-    if (p.ttail > 0 || p.n_heavy > 0) {
+    if (!LEAN && (p.ttail > 0 || p.n_heavy > 0)) {
       unit_query_rows(p, ms.qo, rg, bb, hh, ctid, (CW * 32));
       named_bar_sync(1, (CW * 32));
       unit_codec_rows(p, ms.qo, ms.qc, ctid, (CW * 32));
@@ -902,7 +902,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
       }
       const bool aborted = ms.abort != 0;
       uint8_t* st = smem + (size_t)s * p.stage_bytes;
-      const bool compressed = lt < p.n_ct;
+      const bool compressed = LEAN ? true : lt < p.n_ct;
       const int t0 = (compressed ? lt : lt - p.n_ct) * TILE;
       const int rem_ = static_cast<int>(compressed ? p.tc : p.ttail) - t0;
       const int len = rem_ < TILE ? rem_ : TILE;
@@ -1026,7 +1026,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
             s0[half * 4 + 3] += hv.w;
           }
           __syncwarp();  // scratch reads done before the P store
-        } else if (p.n_heavy) {
+        } else if (!LEAN && p.n_heavy) {
           const uint16_t* h0 = reinterpret_cast<const uint16_t*>(st + heavy_off) + (size_t)tok0 * p.n_heavy * p.bd;
           const uint16_t* h1 = reinterpret_cast<const uint16_t*>(st + heavy_off) + (size_t)tok1 * p.n_heavy * p.bd;
           for (int hj = 0; hj < p.n_heavy; ++hj) {
@@ -1778,6 +1778,14 @@ int launch_decode(const DecodeParams& p, const CUtensorMap& mv, const CUtensorMa
   if (kHv && hv)
     kern = cw == 12 ? (nb16 ? decode_attn_kernel<R, D, 16, 12, kHv> : decode_attn_kernel<R, D, 0, 12, kHv>)
                     : (nb16 ? decode_attn_kernel<R, D, 16, 8, kHv> : decode_attn_kernel<R, D, 0, 8, kHv>);
+  // Lean variants for the two streaming formats of the batched workloads
+  // (compressed tokens only, no heavy blocks, no masks): every other branch
+  // is compiled out, which frees registers and issue slots per tile.
+  if constexpr (R == 4 && D == 128) {
+    const bool plain = nb16 && !hv && p.n_heavy == 0 && p.n_tt == 0 && !p.causal && p.mask == nullptr;
+    if (plain && p.vdec == 0 && cw == 8) kern = decode_attn_kernel<R, D, 16, 8, false, 1>;
+    if (plain && p.vdec == 4 && cw == 12) kern = decode_attn_kernel<R, D, 16, 12, false, 2>;
+  }
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess)
