@@ -330,13 +330,28 @@ __global__ void __launch_bounds__(256) lut_block_kernel(const __grid_constant__ 
   __shared__ __align__(16) float qs[kLutUnits][R][BD];
   const int tid = threadIdx.x;
   const int b = blockIdx.x;
+  // This kernel is launched as a programmatic dependent of the kernel before
+  // it (typically the previous step's decode, which signals at its start):
+  // before griddepcontrol.wait it reads only codec state (centroids,
+  // permutation, heavy-block mask), which no kernel that signals early writes.
   if ((int)blockIdx.y >= p.lut_groups) {  // fused cache append
     grid_launch_dependents();
+    grid_dependency_wait();  // the cache streams may still be read before this
     append_rows<BD>(p, b, (int64_t)blockIdx.y - p.lut_groups);
     return;
   }
   const int64_t u0 = (int64_t)blockIdx.y * kLutUnits;
   grid_launch_dependents();  // let the decode grid start streaming now
+  const int c = tid;
+  const bool zero = p.n_heavy > 0 && p.heavy && p.heavy[b];
+  float cv[BD];
+#pragma unroll
+  for (int j = 0; j < BD; j += 4) {
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (c < p.k) v = __ldg(reinterpret_cast<const float4*>(p.cents + ((size_t)b * p.k + c) * BD + j));
+    cv[j] = v.x; cv[j + 1] = v.y; cv[j + 2] = v.z; cv[j + 3] = v.w;
+  }
+  grid_dependency_wait();  // queries, and the table slots the previous decode reads
   const float sc = round_to(p.scale, p.qdt);
   const int rows_valid = p.nrep * p.tq;
   for (int e = tid; e < kLutUnits * R * BD; e += 256) {
@@ -357,15 +372,6 @@ __global__ void __launch_bounds__(256) lut_block_kernel(const __grid_constant__ 
       }
     }
     qs[ui][r][j] = v;
-  }
-  const int c = tid;
-  const bool zero = p.n_heavy > 0 && p.heavy && p.heavy[b];
-  float cv[BD];
-#pragma unroll
-  for (int j = 0; j < BD; j += 4) {
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (c < p.k) v = __ldg(reinterpret_cast<const float4*>(p.cents + ((size_t)b * p.k + c) * BD + j));
-    cv[j] = v.x; cv[j + 1] = v.y; cv[j + 2] = v.z; cv[j + 3] = v.w;
   }
   __syncthreads();
   if (c >= p.k) return;
@@ -576,6 +582,9 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
   Misc& ms = *reinterpret_cast<Misc*>(smem + p.off_misc);
   float* lut = reinterpret_cast<float*>(smem + p.off_lut);
 
+  // The next step's table kernel may launch now: it waits for this grid
+  // before it reads or writes anything this grid uses.
+  grid_launch_dependents();
   const int64_t cta = blockIdx.x;
   const Sched sched = make_sched(p.total_tiles, p.tpu, p.w_unit, p.grid);
   const int64_t t_begin = range_start(sched, cta);
@@ -1756,8 +1765,21 @@ int launch_decode(const DecodeParams& p, const CUtensorMap& mv, const CUtensorMa
   }
   if (p.rot_k == nullptr && (p.bd == 8 || p.bd == 4) && p.k <= 256) {
     const dim3 bgrid(static_cast<unsigned>(p.nb), static_cast<unsigned>(p.lut_groups + p.app_groups));
-    if (p.bd == 8) lut_block_kernel<R, 8><<<bgrid, 256, 0, st>>>(p);
-    else lut_block_kernel<R, 4><<<bgrid, 256, 0, st>>>(p);
+    // programmatic dependent of the previous kernel in the stream (the
+    // kernel waits for it before touching anything but codec state)
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = bgrid;
+    lc.blockDim = dim3(256);
+    lc.stream = st;
+    cudaLaunchAttribute la[1];
+    la[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    la[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = la;
+    lc.numAttrs = 1;
+    const cudaError_t le = p.bd == 8 ? cudaLaunchKernelEx(&lc, lut_block_kernel<R, 8>, p)
+                                     : cudaLaunchKernelEx(&lc, lut_block_kernel<R, 4>, p);
+    if (le != cudaSuccess)
+      return fail(SS_ERR_CUDA, std::string("ss_decode_attn: table launch: ") + cudaGetErrorString(le));
   } else if (p.bd == 8) {
     lut_kernel<R, 8><<<lgrid, kLutThreads, 0, st>>>(p);
   } else if (p.bd == 4) {
