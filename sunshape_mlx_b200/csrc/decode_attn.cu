@@ -110,7 +110,7 @@ struct DecodeParams {
   const void* app_v;
   int app_dt;
   int64_t app_kps, app_krs, app_vps, app_vrs, app_rows;
-  int app_groups;           // 32-row append CTAs per key block
+  int app_groups;           // 8-row append CTAs per key block
   int lut_groups;           // table CTAs per key block (grid.y below the append CTAs)
   uint16_t* v_w;            // fp16 value stream (append writes)
   int* counters;
@@ -238,57 +238,63 @@ __device__ __forceinline__ void unit_codec_rows(const DecodeParams& p, const flo
 // the permutation, fused multiply-adds in dim order, zero for pass-through
 // blocks.
 constexpr int kLutUnits = 4;
-// Fused cache append, one CTA per (key block b, 32 appended rows): lane =
-// row, warp w scans centroids [w * per, (w + 1) * per) in order with a
-// strict '<' and the warps' winners are combined in warp order -- the first
-// index whose distance is below every earlier one, as the reference's
-// sequential loop and ss_cache_append (a NaN distance at index 0 keeps 0).
-// Distances in NumPy's order (dist_direct). Heavy blocks store the fp16
-// key values and index 0. CTAs of block 0 also store the value rows.
+// Fused cache append, one CTA per (key block b, 8 appended rows): warp w
+// quantizes row 8a + w, lane l scans centroids l, l + 32, ... (up to 256) in
+// order with a strict '<', and the lanes' winners are combined by (distance,
+// index) -- the first index whose distance is below every earlier one, as the
+// reference's sequential loop and ss_cache_append (NaN distances never win; a
+// NaN distance at index 0, or no finite distance, gives index 0). Distances
+// in NumPy's order (dist_direct). Heavy blocks store the fp16 key values and
+// index 0. CTAs of block 0 also store the value rows.
+constexpr int kAppRows = 8;
 template <int BD>
 __device__ __forceinline__ void append_rows(const DecodeParams& p, int b, int64_t a) {
+  __shared__ float s_krow[kAppRows][129];  // the rows' keys, original basis
+  __shared__ int s_col[BD];
   __shared__ __align__(16) float s_c[256 * BD];
-  __shared__ float s_best[8][32];
-  __shared__ int s_bi[8][32];
-  __shared__ float s_d0[32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t n_rows = (int64_t)p.b * p.hkv * p.app_rows;
-  const int64_t r = a * 32 + lane;
+  const int64_t r = a * kAppRows + warp;
   const bool valid = r < n_rows;
   int64_t pair = 0, tt = 0;
   if (valid) { pair = r / p.app_rows; tt = r - pair * p.app_rows; }
   const int64_t pos = p.tc - p.app_rows + tt;
-  float kk[BD];
-#pragma unroll
-  for (int j = 0; j < BD; ++j) {
-    const int col = b * BD + j;
-    kk[j] = valid ? load_as_f32(p.app_k, p.app_dt, pair * p.app_kps + tt * p.app_krs +
-                                                       (p.perm ? __ldg(p.perm + col) : col))
-                  : 0.f;
+  const bool heavy = p.n_heavy > 0 && p.heavy && p.heavy[b];
+  // Every global read is issued before the barrier (the warp's key row, the
+  // block's permutation, this lane's centroids, value rows): the CTA waits
+  // for one memory latency.
+  if (tid < BD) s_col[tid] = p.perm ? __ldg(p.perm + b * BD + tid) : b * BD + tid;
+  const int64_t kbase = pair * p.app_kps + tt * p.app_krs;
+  for (int j = lane; j < p.d; j += 32)
+    s_krow[warp][j] = valid ? load_as_f32(p.app_k, p.app_dt, kbase + j) : 0.f;
+  constexpr int kPer = 8;  // centroids per lane (256 / 32)
+  if (!heavy) {
+    const float* cb = p.cents + (size_t)b * p.k * BD;
+    for (int e = tid * 4; e < p.k * BD; e += 1024)
+      *reinterpret_cast<float4*>(s_c + e) = __ldg(reinterpret_cast<const float4*>(cb + e));
   }
-  if (b == 0) {
-    // the value rows of these 32 tokens, as fp16, in 8-element chunks whose
-    // loads all issue before their stores (source and destination may alias
-    // as far as the compiler knows)
-    const int cpr = p.d / 8;
-    for (int e = tid; e < 32 * cpr; e += 256) {
-      const int rr = e / cpr, j0 = (e - rr * cpr) * 8;
-      const int64_t ro = a * 32 + rr;
-      if (ro >= n_rows) continue;
-      const int64_t pr = ro / p.app_rows, tr = ro - pr * p.app_rows;
-      const int64_t src = pr * p.app_vps + tr * p.app_vrs + j0;
+  if (b == 0 && valid) {
+    // this warp's value row, as fp16, in 8-element chunks whose loads all
+    // issue before their stores (source and destination may alias as far as
+    // the compiler knows)
+    const int64_t src0 = pair * p.app_vps + tt * p.app_vrs;
+    for (int j0 = lane * 8; j0 < p.d; j0 += 256) {
       float x[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) x[j] = load_as_f32(p.app_v, p.app_dt, src + j);
+      for (int j = 0; j < 8; ++j) x[j] = load_as_f32(p.app_v, p.app_dt, src0 + j0 + j);
       uint4 h;
       h.x = pack_h2(x[0], x[1]); h.y = pack_h2(x[2], x[3]);
       h.z = pack_h2(x[4], x[5]); h.w = pack_h2(x[6], x[7]);
-      *reinterpret_cast<uint4*>(p.v_w + pr * p.v_ps + (p.tc - p.app_rows + tr) * p.d + j0) = h;
+      *reinterpret_cast<uint4*>(p.v_w + pair * p.v_ps + pos * p.d + j0) = h;
     }
   }
-  const bool heavy = p.n_heavy > 0 && p.heavy && p.heavy[b];
+  __syncthreads();
+  if (!valid) return;
+  float kk[BD];
+#pragma unroll
+  for (int j = 0; j < BD; ++j) kk[j] = s_krow[warp][s_col[j]];
   if (heavy) {
-    if (warp == 0 && valid) {
+    if (lane == 0) {
       int hpos = 0;
       for (int bb = 0; bb < b; ++bb) hpos += p.heavy[bb] ? 1 : 0;
       uint16_t* dst = const_cast<uint16_t*>(p.kheavy) + pair * p.kh_ps +
@@ -299,34 +305,32 @@ __device__ __forceinline__ void append_rows(const DecodeParams& p, int b, int64_
     }
     return;
   }
-  const float* cb = p.cents + (size_t)b * p.k * BD;
-  for (int e = tid; e < p.k * BD; e += 256) s_c[e] = __ldg(cb + e);
-  __syncthreads();
-  const int per = (p.k + 7) / 8;
-  const int c0 = warp * per, c1 = min(p.k, c0 + per);
+  float dd[kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int c = lane + 32 * i;
+    dd[i] = c < p.k ? dist_direct<BD>(kk, s_c + c * BD) : 0.f;
+  }
   float best = __int_as_float(0x7f800000);
   int bi = 0x7fffffff;
-  for (int c = c0; c < c1; ++c) {
-    const float dd = dist_direct<BD>(kk, s_c + c * BD);
-    if (c == 0) s_d0[lane] = dd;
-    if (dd < best) { best = dd; bi = c; }
+#pragma unroll
+  for (int i = 0; i < kPer; ++i)
+    if (lane + 32 * i < p.k && dd[i] < best) { best = dd[i]; bi = lane + 32 * i; }
+  const float d0 = __shfl_sync(0xffffffffu, dd[0], 0);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ob < best || (ob == best && oi < bi)) { best = ob; bi = oi; }
   }
-  s_best[warp][lane] = best;
-  s_bi[warp][lane] = bi;
-  __syncthreads();
-  if (warp == 0 && valid) {
-    float bv = s_best[0][lane];
-    int bx = s_bi[0][lane];
-    for (int w = 1; w < 8; ++w)
-      if (s_best[w][lane] < bv) { bv = s_best[w][lane]; bx = s_bi[w][lane]; }
-    const float d0 = s_d0[lane];
-    const int idx = (d0 != d0 || bx == 0x7fffffff) ? 0 : bx;
+  if (lane == 0) {
+    const int idx = (d0 != d0 || bi == 0x7fffffff) ? 0 : bi;
     const_cast<uint8_t*>(p.idx)[pair * p.idx_ps + pos * p.nb + b] = static_cast<uint8_t>(idx);
   }
 }
 
 template <int R, int BD>
-__global__ void __launch_bounds__(256) lut_block_kernel(const __grid_constant__ DecodeParams p) {
+__global__ void __launch_bounds__(256, 4) lut_block_kernel(const __grid_constant__ DecodeParams p) {
   __shared__ __align__(16) float qs[kLutUnits][R][BD];
   const int tid = threadIdx.x;
   const int b = blockIdx.x;
@@ -1956,7 +1960,7 @@ int run_decode(const ss_decode_args* a, float* part_out, void* stream,
     p.app_kps = a->app_key_pair_stride; p.app_krs = a->app_key_row_stride;
     p.app_vps = a->app_value_pair_stride; p.app_vrs = a->app_value_row_stride;
     p.app_rows = a->app_rows;
-    p.app_groups = static_cast<int>((rows + 31) / 32);
+    p.app_groups = static_cast<int>((rows + kAppRows - 1) / kAppRows);
     p.v_w = const_cast<uint16_t*>(reinterpret_cast<const uint16_t*>(a->v));
     count_dispatch("ss_cache_append (fused into ss_decode_attn)");
   }
