@@ -748,6 +748,22 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
   const int rows_valid = p.nrep * p.tq;
   const bool per_token_mask = LEAN ? false : (p.causal || p.mask != nullptr);
   const int vdec = LEAN == 1 ? 0 : LEAN == 2 ? 4 : p.vdec;
+  // LEAN 2: the four levels of the 2-bit codes split into fp16 heads and
+  // fp16 remainders (level = head + remainder to ~2^-22), as byte-permute
+  // sources: low bytes of levels 0..3 in *_lo, high bytes in *_hi
+  uint32_t lv_lo = 0, lv_hi = 0, lw_lo = 0, lw_hi = 0;
+  if constexpr (LEAN == 2) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const __half hh = __float2half_rn(p.levels[c]);
+      const uint32_t h = __half_as_ushort(hh);
+      const uint32_t l = __half_as_ushort(__float2half_rn(p.levels[c] - __half2float(hh)));
+      lv_lo |= (h & 0xffu) << (8 * c);
+      lv_hi |= (h >> 8) << (8 * c);
+      lw_lo |= (l & 0xffu) << (8 * c);
+      lw_hi |= (l >> 8) << (8 * c);
+    }
+  }
   // vdec 4: this lane's byte offsets (from the stage base, first 16-token
   // step) of its four packed value words and of its two fp16 group scales
   const uint32_t q4_word_off =
@@ -1190,6 +1206,83 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
             ldsm_x4_trans(vb + ks * 2048 + col, x0, x1, x2, x3);
             if constexpr (R == 8) mma_16816(acc[mt], x0, x1, x2, x3, c0, c1);
             mma_16816(acc[mt], x0, x1, x2, x3, b0, b1);
+          }
+        }
+      } else if constexpr (LEAN == 2) {
+        // 2-bit codes with fp16 scales per 32 channels, decoded straight into
+        // the MMA's A fragments (no staging tile, no level-table loads).
+        // Fragment register (dim d, tokens k, k + 1) of lane (g, t): dims
+        // 16 mt + g and 16 mt + g + 8 are codes g and g + 8 of packed word mt
+        // of a token; one byte permute takes the bytes holding them from the
+        // two tokens' words, a shift and mask isolate the four codes, one
+        // multiply-add turns them into two byte-permute selectors that pick
+        // fp16 levels (low bytes in lv_lo, high bytes in lv_hi), and an fp16x2
+        // multiply applies the two tokens' group scales.
+        const int g = lane >> 2, t = lane & 3;
+        const uint32_t zsel = (uint32_t)(g >> 2) * 0x1111u + 0x6240u;
+        const uint32_t csh = 2u * (uint32_t)(g & 3);
+        const uint32_t sbase = smem_u32(st) + p.off_aux;
+#pragma unroll
+        for (int ks = 0; ks < SL / 16; ++ks) {
+          const int tok = slice * SL + ks * 16 + 2 * t;  // tokens tok, tok+1, tok+8, tok+9
+          uint32_t sc2[2][4];  // [token pair][group]: (scale of the first, of the second)
+#pragma unroll
+          for (int pr = 0; pr < 2; ++pr) {
+            uint32_t a0, a1, b0_, b1_;
+            const uint32_t sa = sbase + TILE * 32 + (uint32_t)(tok + 8 * pr) * 8u;
+            asm("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(a0), "=r"(a1) : "r"(sa));
+            asm("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(b0_), "=r"(b1_) : "r"(sa + 8u));
+            // tokens past the end: zero scale, so whatever their stage bytes
+            // hold, they contribute exactly 0 (their weights are 0 too)
+            if (tok + 8 * pr >= len) a0 = a1 = 0u;
+            if (tok + 8 * pr + 1 >= len) b0_ = b1_ = 0u;
+            sc2[pr][0] = __byte_perm(a0, b0_, 0x5410);
+            sc2[pr][1] = __byte_perm(a0, b0_, 0x7632);
+            sc2[pr][2] = __byte_perm(a1, b1_, 0x5410);
+            sc2[pr][3] = __byte_perm(a1, b1_, 0x7632);
+          }
+          uint32_t bp0, bp1, cp0 = 0, cp1 = 0;
+          ldsm_x2_trans(pw_addr + ks * 256, bp0, bp1);
+          if constexpr (R == 8) ldsm_x2_trans(pwl_addr + ks * 256, cp0, cp1);
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            uint32_t w[2][2][4];  // [token pair][first, second token][word]
+#pragma unroll
+            for (int pr = 0; pr < 2; ++pr)
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const uint32_t wa = sbase + (uint32_t)(tok + 8 * pr + e) * 32u + half * 16u;
+                asm("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                    : "=r"(w[pr][e][0]), "=r"(w[pr][e][1]), "=r"(w[pr][e][2]), "=r"(w[pr][e][3])
+                    : "r"(wa));
+              }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int mt = half * 4 + i;
+              uint32_t fr[2][2];  // [token pair][dim g, dim g + 8]
+#pragma unroll
+              for (int pr = 0; pr < 2; ++pr) {
+                const uint32_t z = __byte_perm(w[pr][0][i], w[pr][1][i], zsel);
+                const uint32_t c4 = (z >> csh) & 0x03030303u;
+                const uint32_t sel = c4 * 0x11u + 0x40404040u;
+                const uint32_t sc = sc2[pr][mt >> 1];
+#pragma unroll
+                for (int d8 = 0; d8 < 2; ++d8) {
+                  const uint32_t sl = d8 ? sel >> 16 : sel;
+                  // level = h + l (fp16 head and remainder): fp16(h s + fp16(l s))
+                  // is the reference's fp16(level * scale) up to rare near-ties
+                  const uint32_t h = __byte_perm(lv_lo, lv_hi, sl);
+                  const uint32_t l = __byte_perm(lw_lo, lw_hi, sl);
+                  uint32_t ls;
+                  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(ls) : "r"(l), "r"(sc));
+                  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(fr[pr][d8]) : "r"(h), "r"(sc), "r"(ls));
+                }
+              }
+              // a0 (dim g, tokens 2t..), a1 (dim g+8, tokens 2t..), a2 (dim g,
+              // tokens 2t+8..), a3 (dim g+8, tokens 2t+8..)
+              if constexpr (R == 8) mma_16816(acc[mt], fr[0][0], fr[0][1], fr[1][0], fr[1][1], cp0, cp1);
+              mma_16816(acc[mt], fr[0][0], fr[0][1], fr[1][0], fr[1][1], bp0, bp1);
+            }
           }
         }
       } else {
@@ -1701,7 +1794,7 @@ int make_plan_r(const ss_decode_args* a, Plan& pl, int r_cap, int cw) {
   if (fixed + 2 * (size_t)pl.stage_bytes > kSmemBudget)
     return fail(SS_ERR_UNSUPPORTED, "ss_decode_attn: configuration exceeds shared memory");
   int stages = static_cast<int>((kSmemBudget - fixed) / pl.stage_bytes);
-  if (stages > 6) stages = 6;
+  if (stages > (cw == 16 ? 8 : 6)) stages = cw == 16 ? 8 : 6;
   // The consumer warps form tile groups that take tiles round robin; a warp may
   // only wait for the barrier phase right after the one it consumed last,
   // which holds when the stage count is a multiple of the number of groups.
@@ -1744,7 +1837,15 @@ int make_plan_r(const ss_decode_args* a, Plan& pl, int r_cap, int cw) {
 int make_plan(const ss_decode_args* a, Plan& pl) {
   int rc = SS_ERR_UNSUPPORTED;
   for (int r_cap = 8;;) {
-    for (int cw : {12, 8}) {
+    // 16 consumer warps only for the lean 2-bit-value kernel (4 rows, 16
+    // key blocks, compressed tokens only): its per-token work is latency
+    // bound and the small stages leave room for a fourth tile group
+    const bool q16 = a->vfmt == SS_V_QUANT && a->d == 128 && a->v_bits == 2 &&
+                     a->v_group == 32 && a->v_scale_dtype == SS_F16 && !a->v_zeros &&
+                     a->d / a->bd == 16 && a->k == 256 && a->n_heavy == 0 && a->ttail == 0 &&
+                     !a->causal && a->mask == nullptr && a->hq / a->hkv * a->tq == 4;
+    for (int cw : {16, 12, 8}) {
+      if (cw == 16 && !q16) continue;
       rc = make_plan_r(a, pl, r_cap, cw);
       if (rc != SS_ERR_UNSUPPORTED) return rc;
     }
@@ -1807,11 +1908,18 @@ int launch_decode(const DecodeParams& p, const CUtensorMap& mv, const CUtensorMa
   // Lean variants for the two streaming formats of the batched workloads
   // (compressed tokens only, no heavy blocks, no masks): every other branch
   // is compiled out, which frees registers and issue slots per tile.
+  bool lean16 = false;
   if constexpr (R == 4 && D == 128) {
     const bool plain = nb16 && !hv && p.n_heavy == 0 && p.n_tt == 0 && !p.causal && p.mask == nullptr;
     if (plain && p.vdec == 0 && cw == 8) kern = decode_attn_kernel<R, D, 16, 8, false, 1>;
     if (plain && p.vdec == 4 && cw == 12) kern = decode_attn_kernel<R, D, 16, 12, false, 2>;
+    if (plain && p.vdec == 4 && cw == 16) {
+      kern = decode_attn_kernel<R, D, 16, 16, false, 2>;
+      lean16 = true;
+    }
   }
+  if (cw == 16 && !lean16)
+    return fail(SS_ERR_UNSUPPORTED, "ss_decode_attn: 16 consumer warps need the lean 2-bit kernel");
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess)
