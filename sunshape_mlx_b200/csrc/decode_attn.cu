@@ -1218,32 +1218,41 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
         // multiply-add turns them into two byte-permute selectors that pick
         // fp16 levels (low bytes in lv_lo, high bytes in lv_hi), and an fp16x2
         // multiply applies the two tokens' group scales.
+        // MMA k slot kappa of a 16-token step holds token pi(kappa) =
+        // (kappa & 8) + ((kappa & 7) >> 1) + 4 (kappa & 1), for A and B alike
+        // (a sum over tokens does not depend on their order): lane t's four
+        // tokens are then t, t + 4, t + 8, t + 12, so the four lanes that load
+        // one token slot read four consecutive tokens (distinct banks).
         const int g = lane >> 2, t = lane & 3;
         const uint32_t zsel = (uint32_t)(g >> 2) * 0x1111u + 0x6240u;
+        const int kap = lane & 15;
+        const uint32_t pw_perm = smem_u32(Pw) + (uint32_t)((kap & 8) + ((kap & 7) >> 1) + 4 * (kap & 1)) * 16u;
+        const uint32_t pwl_perm = smem_u32(Pw_lo) + (uint32_t)((kap & 8) + ((kap & 7) >> 1) + 4 * (kap & 1)) * 16u;
         const uint32_t csh = 2u * (uint32_t)(g & 3);
         const uint32_t sbase = smem_u32(st) + p.off_aux;
 #pragma unroll
         for (int ks = 0; ks < SL / 16; ++ks) {
-          const int tok = slice * SL + ks * 16 + 2 * t;  // tokens tok, tok+1, tok+8, tok+9
+          const int tok = slice * SL + ks * 16 + t;  // tokens tok, tok+4, tok+8, tok+12
           uint32_t sc2[2][4];  // [token pair][group]: (scale of the first, of the second)
 #pragma unroll
           for (int pr = 0; pr < 2; ++pr) {
             uint32_t a0, a1, b0_, b1_;
             const uint32_t sa = sbase + TILE * 32 + (uint32_t)(tok + 8 * pr) * 8u;
             asm("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(a0), "=r"(a1) : "r"(sa));
-            asm("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(b0_), "=r"(b1_) : "r"(sa + 8u));
-            // tokens past the end: zero scale, so whatever their stage bytes
-            // hold, they contribute exactly 0 (their weights are 0 too)
+            asm("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(b0_), "=r"(b1_) : "r"(sa + 32u));
+            // tokens past the end (relative to the tile): zero scale, so
+            // whatever their stage bytes hold, they contribute exactly 0
+            // (their weights are 0 too)
             if (tok + 8 * pr >= len) a0 = a1 = 0u;
-            if (tok + 8 * pr + 1 >= len) b0_ = b1_ = 0u;
+            if (tok + 8 * pr + 4 >= len) b0_ = b1_ = 0u;
             sc2[pr][0] = __byte_perm(a0, b0_, 0x5410);
             sc2[pr][1] = __byte_perm(a0, b0_, 0x7632);
             sc2[pr][2] = __byte_perm(a1, b1_, 0x5410);
             sc2[pr][3] = __byte_perm(a1, b1_, 0x7632);
           }
           uint32_t bp0, bp1, cp0 = 0, cp1 = 0;
-          ldsm_x2_trans(pw_addr + ks * 256, bp0, bp1);
-          if constexpr (R == 8) ldsm_x2_trans(pwl_addr + ks * 256, cp0, cp1);
+          ldsm_x2_trans(pw_perm + ks * 256, bp0, bp1);
+          if constexpr (R == 8) ldsm_x2_trans(pwl_perm + ks * 256, cp0, cp1);
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
             uint32_t w[2][2][4];  // [token pair][first, second token][word]
@@ -1251,7 +1260,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
             for (int pr = 0; pr < 2; ++pr)
 #pragma unroll
               for (int e = 0; e < 2; ++e) {
-                const uint32_t wa = sbase + (uint32_t)(tok + 8 * pr + e) * 32u + half * 16u;
+                const uint32_t wa = sbase + (uint32_t)(tok + 8 * pr + 4 * e) * 32u + half * 16u;
                 asm("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
                     : "=r"(w[pr][e][0]), "=r"(w[pr][e][1]), "=r"(w[pr][e][2]), "=r"(w[pr][e][3])
                     : "r"(wa));
