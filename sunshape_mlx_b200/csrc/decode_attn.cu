@@ -955,9 +955,18 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
 #pragma unroll
           for (int i = 0; i < R / 2; ++i) acc2[i] = 0ull;
           const uint32_t lbase = smem_u32(lut);
+          // the token's index bytes in one 16-byte load per 16 blocks (lanes
+          // read consecutive 16-byte rows: no bank conflicts)
+          uint32_t cw4[NBC / 4];
+#pragma unroll
+          for (int w = 0; w < NBC / 4; w += 4) {
+            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+            if (v0) v = *reinterpret_cast<const uint4*>(ir0 + 4 * w);
+            cw4[w] = v.x; cw4[w + 1] = v.y; cw4[w + 2] = v.z; cw4[w + 3] = v.w;
+          }
 #pragma unroll
           for (int w = 0; w < NBC / 4; ++w) {
-            const uint32_t c0w = v0 ? reinterpret_cast<const uint32_t*>(ir0)[w] : 0u;
+            const uint32_t c0w = cw4[w];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               const uint32_t a = lbase + ((4 * w + j) * 256u * R + __byte_perm(c0w, 0u, 0x4440u + j) * R) * 4u;
