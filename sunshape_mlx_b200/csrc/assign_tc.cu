@@ -13,12 +13,12 @@
 //
 // with x = xh + xl the fp16 hi/lo split of a float32 value, after scaling the
 // block by a power of two so that its largest centroid component is in [1, 2).
-// The epilogue (one thread per row) reads the row's V twice from TMEM: pass 1
-// takes the minimum s1 (three-input min, ALU pipe); pass 2 (FMA pipe)
-// evaluates e(c) = sat((s1 + T - V(c)) * 4/T), which is exactly 1 at the
-// minimum and exactly 0 for every V(c) >= s1 + T, and sums e and e * c.
-// A count of exactly 1 means no other centroid lies within T of the minimum,
-// and the summed position is the winner's index. Error analysis (u = 2^-24,
+// The epilogue (one thread per row) reads the row's V once from TMEM and
+// keeps the minima of two partitions of the columns (by high and by low
+// nibble of the centroid index; three-input mins, ALU pipe). A single group
+// below s1 + T in each partition means no other centroid lies within T of
+// the minimum s1 (two distinct indices differ in a nibble), and the two
+// groups give the winner's index. Error analysis (u = 2^-24,
 // S = ||k||^2 + max_c ||c||^2, all in scaled units, per value; a comparison
 // of two values doubles each term):
 //   |reference distance - exact real distance| <= 2^-19 S (either mode),
@@ -169,12 +169,6 @@ struct TcShape {
   static constexpr int kKt = ((3 * BD + 2) + 15) / 16 * 16;  // K of the MMA chain
 };
 
-// fma with the result clamped to [0, 1] (NaN -> 0), on the FMA pipe.
-__device__ __forceinline__ float fma_sat(float a, float b, float c) {
-  float r;
-  asm("fma.rn.sat.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
-  return r;
-}
 
 __device__ __forceinline__ float fmin3(float a, float b, float c) {
   float r;
@@ -578,84 +572,57 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(kn_empty + n % kKnRing);
         if (!heavy) {
-          // Pass 1 (ALU pipe): the minimum V of every 32-column chunk (one
-          // three-input min per two columns); chunk pairs per TMEM wait.
+          // One pass over the row's V (ALU pipe): the minima of two partitions
+          // of the columns, ma[c >> 4] (16 runs of 16 columns) and mb[c & 15]
+          // (16 residue classes), one three-input min per two columns each.
+          // Two distinct columns differ in their high or low nibble, so some
+          // other column lies within T of the minimum s1 exactly when, in one
+          // of the partitions, a second group's minimum is below s1 + T. If
+          // each partition has a single group below it, the winner is the
+          // column (that ma group, that mb group).
           const float inf = __int_as_float(0x7f800000);
-          float cmin[8];
+          float ma[16], mb[16];
+#pragma unroll
+          for (int q = 0; q < 16; ++q) { ma[q] = inf; mb[q] = inf; }
 #pragma unroll
           for (int ch = 0; ch < 8; ch += 2) {
-            cmin[ch] = inf;
-            cmin[ch + 1] = inf;
             if (ch < nch) {
               uint32_t v0[32], v1[32];
               tc_ld32(tbase + ch * 32, v0);
               tc_ld32(tbase + (ch + 1) * 32, v1);  // nch is even
               tc_wait_ld();
-              float m0 = inf, m1 = inf, m2 = inf, m3 = inf;
+              float a0 = inf, a1 = inf, a2 = inf, a3 = inf;
 #pragma unroll
-              for (int j = 0; j < 32; j += 4) {
-                m0 = fmin3(m0, __uint_as_float(v0[j]), __uint_as_float(v0[j + 1]));
-                m1 = fmin3(m1, __uint_as_float(v1[j]), __uint_as_float(v1[j + 1]));
-                m2 = fmin3(m2, __uint_as_float(v0[j + 2]), __uint_as_float(v0[j + 3]));
-                m3 = fmin3(m3, __uint_as_float(v1[j + 2]), __uint_as_float(v1[j + 3]));
+              for (int j = 0; j < 16; j += 2) {
+                a0 = fmin3(a0, __uint_as_float(v0[j]), __uint_as_float(v0[j + 1]));
+                a1 = fmin3(a1, __uint_as_float(v0[j + 16]), __uint_as_float(v0[j + 17]));
+                a2 = fmin3(a2, __uint_as_float(v1[j]), __uint_as_float(v1[j + 1]));
+                a3 = fmin3(a3, __uint_as_float(v1[j + 16]), __uint_as_float(v1[j + 17]));
               }
-              cmin[ch] = fminf(m0, m2);
-              cmin[ch + 1] = fminf(m1, m3);
+              ma[2 * ch] = a0;
+              ma[2 * ch + 1] = a1;
+              ma[2 * ch + 2] = a2;
+              ma[2 * ch + 3] = a3;
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                mb[j] = fmin3(mb[j], __uint_as_float(v0[j]), __uint_as_float(v0[j + 16]));
+                mb[j] = fmin3(mb[j], __uint_as_float(v1[j]), __uint_as_float(v1[j + 16]));
+              }
             }
           }
           float s1 = inf;
 #pragma unroll
-          for (int q = 0; q < 8; q += 2) s1 = fmin3(s1, cmin[q], cmin[q + 1]);
-          // Pass 2: e = sat((s1 + T - V) * 4/T) is exactly 1 at the minimum and
-          // exactly 0 for every V >= s1 + T (up to rounding of 2^-8 T). The e of
-          // column j of every chunk accumulate into A[j] (packed fp32 pair adds),
-          // so a column costs one saturating FMA and half a packed add.
-          // cnt = sum A == 1 means no other centroid within T of the minimum;
-          // then A is one-hot at the winner's column within its chunk, and its
-          // chunk is the only one whose minimum equals s1.
+          for (int q = 0; q < 16; q += 2) s1 = fmin3(s1, ma[q], ma[q + 1]);
           const float sn = kn + s_cmax[bl];
-          const float tie = sn * kTieRel;
-          const float big = 4.f / tie;
-          const float thr_big = (s1 + tie) * big;
-          float ax[16], ay[16];
-#pragma unroll
-          for (int q = 0; q < 16; ++q) { ax[q] = 0.f; ay[q] = 0.f; }
-          auto sum_chunk = [&](const uint32_t (&v)[32]) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 2) {
-              const float e0 = fma_sat(__uint_as_float(v[j]), -big, thr_big);
-              const float e1 = fma_sat(__uint_as_float(v[j + 1]), -big, thr_big);
-              add_f32x2(ax[j / 2], ay[j / 2], e0, e1);
-            }
-          };
-          {
-            // chunk pairs double-buffered: the next TMEM load is in flight
-            // while the current chunk is summed
-            uint32_t va[32], vb[32];
-            tc_ld32(tbase, va);
-            tc_wait_ld();
-#pragma unroll 1
-            for (int ch = 0; ch < nch; ch += 2) {
-              tc_ld32(tbase + (ch + 1) * 32, vb);  // nch is even
-              sum_chunk(va);
-              tc_wait_ld();
-              if (ch + 2 < nch) tc_ld32(tbase + (ch + 2) * 32, va);
-              sum_chunk(vb);
-              tc_wait_ld();
-            }
-          }
-          float cnt = 0.f, pos = 0.f;
+          const float thr = s1 + sn * kTieRel;
+          int na = 0, nbm = 0, wa = 0, wb = 0;
 #pragma unroll
           for (int q = 0; q < 16; ++q) {
-            cnt += ax[q] + ay[q];
-            pos = fmaf(ax[q], (float)(2 * q), fmaf(ay[q], (float)(2 * q + 1), pos));
+            if (ma[q] < thr) { ++na; wa = q; }
+            if (mb[q] < thr) { ++nbm; wb = q; }
           }
-          int wch = 0;
-#pragma unroll
-          for (int q = 7; q >= 0; --q)
-            if (cmin[q] == s1) wch = q;
-          need = valid && !(cnt == 1.f && sn >= s_slo[bl] && sn <= s_shi[bl]);
-          idx = min(max(wch * 32 + (int)rintf(pos), 0), p.k - 1);
+          need = valid && !(na == 1 && nbm == 1 && sn >= s_slo[bl] && sn <= s_shi[bl]);
+          idx = min(wa * 16 + wb, p.k - 1);
         }
         tc_fence_before();
         __syncwarp();
