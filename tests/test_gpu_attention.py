@@ -212,6 +212,43 @@ def test_quantized_values_decode_vs_torch(ss):
         assert G.rel_err(out, want) < 2e-3, (kind, G.rel_err(out, want))
 
 
+@pytest.mark.parametrize("T", [77, 129, 3000])
+def test_tq_group32_fragment_decode_ragged(ss, T):
+    """2-bit values with fp16 scales per 32 channels, 4 query rows per kv-head:
+    the kernel decodes the codes straight into the P.V MMA fragments. Ragged
+    lengths leave a partial last tile, and the rows past the end hold NaN
+    scales: those tokens must contribute exactly nothing. Checked per element
+    against float64 attention over the values as the kernel rounds them
+    (fp16(level * scale) in the rotated basis), rotated back."""
+    from sunshape_mlx_b200.attention import _run_decode
+
+    B, H, D = 2, 4, 128
+    cents, perm, idx, _, cap = _random_cache_setup(B, H, T, seed=70 + T)
+    vals = torch.randn((B, H, cap, D), device="cuda")
+    codec = ss.TurboQuantValueCodec(head_dim=D, bits=2, group_size=32)
+    p, s = codec.quantize(vals)
+    assert s.dtype == torch.float16 and s.shape[-1] == D // 32
+    s = s.clone()
+    s[:, :, T:] = float("nan")
+    spec = dict(tc=T, cap=cap, idx=idx, vq=p, vs=s, vz=None, bits=2, group=32,
+                levels=codec.levels(None), v_rot=codec.rotation)
+    q = torch.randn((B, 4 * H, 1, D), device="cuda")
+    out = torch.empty_like(q)
+    _run_decode(q, centroids=cents, perm=perm, scale=0.088, spec=spec, causal=False, out=out)
+    # values in the rotated basis, rounded as the kernel rounds them
+    words = p[:, :, :T].to(torch.int64) & 0xFFFFFFFF
+    sh = torch.arange(16, device="cuda", dtype=torch.int64) * 2
+    codes = ((words.unsqueeze(-1) >> sh) & 3).reshape(B, H, T, D)
+    lv = torch.tensor(codec.levels(None)[:4], dtype=torch.float32, device="cuda")
+    r = (lv[codes] * s[:, :, :T].float().repeat_interleave(32, dim=-1)).half()
+    want = _ref_from(cents, perm, idx, r, q, 0.088, T).double() @ codec.rotation.double()
+    err = (out.double() - want).abs()
+    mref = want.abs().max()
+    assert torch.isfinite(out).all()
+    assert float(err.max() / mref) < 1e-3
+    assert float((err / (2e-3 * want.abs() + 1e-4 * mref)).max()) <= 1.0
+
+
 @pytest.mark.parametrize("hq", [8, 16])  # 16: 8 rows per kv-head, tables split into 2 row groups
 def test_mixed_precision_heavy_blocks_exact_scoring(ss, hq):
     rng = np.random.default_rng(4)
