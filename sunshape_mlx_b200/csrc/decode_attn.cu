@@ -355,27 +355,31 @@ __global__ void __launch_bounds__(256, 4) lut_block_kernel(const __grid_constant
     if (c < p.k) v = __ldg(reinterpret_cast<const float4*>(p.cents + ((size_t)b * p.k + c) * BD + j));
     cv[j] = v.x; cv[j + 1] = v.y; cv[j + 2] = v.z; cv[j + 3] = v.w;
   }
-  grid_dependency_wait();  // queries, and the table slots the previous decode reads
-  const float sc = round_to(p.scale, p.qdt);
+  // Each thread's query element (at most one: kLutUnits * R * BD <= 256):
+  // its offset, with the permutation column, is found before the wait (the
+  // permutation is codec state), so only the query load follows it.
+  static_assert(kLutUnits * R * BD <= 256, "one query element per thread");
   const int rows_valid = p.nrep * p.tq;
-  for (int e = tid; e < kLutUnits * R * BD; e += 256) {
-    const int ui = e / (R * BD), rem = e - ui * (R * BD), r = rem / BD, j = rem - r * BD;
+  const int e = tid;
+  const int ui = e / (R * BD), rem = e - ui * (R * BD), r = rem / BD, j = rem - r * BD;
+  int64_t qoff = -1;
+  if (e < kLutUnits * R * BD && u0 + ui < p.n_units) {
     const int64_t u = u0 + ui;
-    float v = 0.f;
-    if (u < p.n_units) {
-      const int64_t pair = u / p.n_rg;
-      const int rg = static_cast<int>(u - pair * p.n_rg);
-      const int bb = static_cast<int>(pair / p.hkv), hh = static_cast<int>(pair % p.hkv);
-      const int rr = rg * R + r;
-      if (rr < rows_valid) {
-        const int rep = rr / p.tq, tqi = rr - rep * p.tq;
-        const int qh = hh * p.nrep + rep;
-        const int col = p.perm ? __ldg(p.perm + b * BD + j) : b * BD + j;
-        v = round_to(load_as_f32(p.q, p.qdt, bb * p.q_sb + qh * p.q_sh + tqi * p.q_st + col) * sc,
-                     p.qdt);
-      }
+    const int64_t pair = u / p.n_rg;
+    const int rg = static_cast<int>(u - pair * p.n_rg);
+    const int bb = static_cast<int>(pair / p.hkv), hh = static_cast<int>(pair % p.hkv);
+    const int rr = rg * R + r;
+    if (rr < rows_valid) {
+      const int rep = rr / p.tq, tqi = rr - rep * p.tq;
+      const int qh = hh * p.nrep + rep;
+      const int col = p.perm ? __ldg(p.perm + b * BD + j) : b * BD + j;
+      qoff = bb * p.q_sb + qh * p.q_sh + tqi * p.q_st + col;
     }
-    qs[ui][r][j] = v;
+  }
+  grid_dependency_wait();  // queries, and the table slots the previous decode reads
+  if (e < kLutUnits * R * BD) {
+    const float sc = round_to(p.scale, p.qdt);
+    qs[ui][r][j] = qoff < 0 ? 0.f : round_to(load_as_f32(p.q, p.qdt, qoff) * sc, p.qdt);
   }
   __syncthreads();
   if (c >= p.k) return;
