@@ -260,19 +260,21 @@ __device__ __forceinline__ void append_rows(const DecodeParams& p, int b, int64_
   if (valid) { pair = r / p.app_rows; tt = r - pair * p.app_rows; }
   const int64_t pos = p.tc - p.app_rows + tt;
   const bool heavy = p.n_heavy > 0 && p.heavy && p.heavy[b];
-  // Every global read is issued before the barrier (the warp's key row, the
-  // block's permutation, this lane's centroids, value rows): the CTA waits
-  // for one memory latency.
+  // Codec state (the block's permutation and centroids) is staged before
+  // griddepcontrol.wait, the step's inputs (key and value rows) after it, all
+  // before the one barrier: the CTA waits for one memory latency after the
+  // previous kernel.
   if (tid < BD) s_col[tid] = p.perm ? __ldg(p.perm + b * BD + tid) : b * BD + tid;
-  const int64_t kbase = pair * p.app_kps + tt * p.app_krs;
-  for (int j = lane; j < p.d; j += 32)
-    s_krow[warp][j] = valid ? load_as_f32(p.app_k, p.app_dt, kbase + j) : 0.f;
   constexpr int kPer = 8;  // centroids per lane (256 / 32)
   if (!heavy) {
     const float* cb = p.cents + (size_t)b * p.k * BD;
     for (int e = tid * 4; e < p.k * BD; e += 1024)
       *reinterpret_cast<float4*>(s_c + e) = __ldg(reinterpret_cast<const float4*>(cb + e));
   }
+  grid_dependency_wait();  // the rows may come from, and the streams be read by, earlier kernels
+  const int64_t kbase = pair * p.app_kps + tt * p.app_krs;
+  for (int j = lane; j < p.d; j += 32)
+    s_krow[warp][j] = valid ? load_as_f32(p.app_k, p.app_dt, kbase + j) : 0.f;
   if (b == 0 && valid) {
     // this warp's value row, as fp16, in 8-element chunks whose loads all
     // issue before their stores (source and destination may alias as far as
@@ -340,8 +342,7 @@ __global__ void __launch_bounds__(256, 4) lut_block_kernel(const __grid_constant
   // permutation, heavy-block mask), which no kernel that signals early writes.
   if ((int)blockIdx.y >= p.lut_groups) {  // fused cache append
     grid_launch_dependents();
-    grid_dependency_wait();  // the cache streams may still be read before this
-    append_rows<BD>(p, b, (int64_t)blockIdx.y - p.lut_groups);
+    append_rows<BD>(p, b, (int64_t)blockIdx.y - p.lut_groups);  // waits inside
     return;
   }
   const int64_t u0 = (int64_t)blockIdx.y * kLutUnits;
