@@ -752,7 +752,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
   for (int m = 0; m < 4; ++m) swz[m] = static_cast<uint32_t>(((2 * m + dsel) ^ mj) << 4);
   const int rows_valid = p.nrep * p.tq;
   const bool per_token_mask = LEAN ? false : (p.causal || p.mask != nullptr);
-  const int vdec = LEAN == 1 ? 0 : LEAN == 2 ? 4 : p.vdec;
+  const int vdec = (LEAN == 1 || LEAN == 3) ? 0 : LEAN == 2 ? 4 : p.vdec;
   // LEAN 2: the four levels of the 2-bit codes split into fp16 heads and
   // fp16 remainders (level = head + remainder to ~2^-22), as byte-permute
   // sources: low bytes of levels 0..3 in *_lo, high bytes in *_hi
@@ -849,7 +849,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
         bulk_g2s(reinterpret_cast<uint8_t*>(lut) + off, src + off,
                  bytes - off < 16384u ? bytes - off : 16384u, &lut_bar);
     }
-    if (!LEAN && (p.ttail > 0 || p.n_heavy > 0)) {
+    if ((!LEAN || LEAN == 3) && (p.ttail > 0 || p.n_heavy > 0)) {
       unit_query_rows(p, ms.qo, rg, bb, hh, ctid, (CW * 32));
       named_bar_sync(1, (CW * 32));
       unit_codec_rows(p, ms.qo, ms.qc, ctid, (CW * 32));
@@ -1069,7 +1069,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
             s0[half * 4 + 3] += hv.w;
           }
           __syncwarp();  // scratch reads done before the P store
-        } else if (!LEAN && p.n_heavy) {
+        } else if ((!LEAN || LEAN == 3) && p.n_heavy) {
           const uint16_t* h0 = reinterpret_cast<const uint16_t*>(st + heavy_off) + (size_t)tok0 * p.n_heavy * p.bd;
           const uint16_t* h1 = reinterpret_cast<const uint16_t*>(st + heavy_off) + (size_t)tok1 * p.n_heavy * p.bd;
           for (int hj = 0; hj < p.n_heavy; ++hj) {
@@ -1932,13 +1932,20 @@ int launch_decode(const DecodeParams& p, const CUtensorMap& mv, const CUtensorMa
   // (compressed tokens only, no heavy blocks, no masks): every other branch
   // is compiled out, which frees registers and issue slots per tile.
   bool lean16 = false;
-  if constexpr (R == 4 && D == 128) {
+  if constexpr ((R == 4 || R == 8) && D == 128) {
     const bool plain = nb16 && !hv && p.n_heavy == 0 && p.n_tt == 0 && !p.causal && p.mask == nullptr;
-    if (plain && p.vdec == 0 && cw == 8) kern = decode_attn_kernel<R, D, 16, 8, false, 1>;
-    if (plain && p.vdec == 4 && cw == 12) kern = decode_attn_kernel<R, D, 16, 12, false, 2>;
-    if (plain && p.vdec == 4 && cw == 16) {
-      kern = decode_attn_kernel<R, D, 16, 16, false, 2>;
-      lean16 = true;
+    if constexpr (R == 4) {
+      if (plain && p.vdec == 0 && cw == 8) kern = decode_attn_kernel<R, D, 16, 8, false, 1>;
+      if (plain && p.vdec == 4 && cw == 12) kern = decode_attn_kernel<R, D, 16, 12, false, 2>;
+      if (plain && p.vdec == 4 && cw == 16) {
+        kern = decode_attn_kernel<R, D, 16, 16, false, 2>;
+        lean16 = true;
+      }
+    } else {
+      // fp16 values with heavy (fp16 pass-through) key blocks on warp MMAs, 8
+      // rows (the long mixed-precision sequence), compressed tokens only, no masks
+      if (nb16 && hv && p.vdec == 0 && p.n_tt == 0 && !p.causal && p.mask == nullptr && cw == 8)
+        kern = decode_attn_kernel<R, D, 16, 8, kHv, 3>;
     }
   }
   if (cw == 16 && !lean16)
