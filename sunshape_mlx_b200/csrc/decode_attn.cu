@@ -752,7 +752,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
   for (int m = 0; m < 4; ++m) swz[m] = static_cast<uint32_t>(((2 * m + dsel) ^ mj) << 4);
   const int rows_valid = p.nrep * p.tq;
   const bool per_token_mask = LEAN ? false : (p.causal || p.mask != nullptr);
-  const int vdec = (LEAN == 1 || LEAN == 3) ? 0 : LEAN == 2 ? 4 : p.vdec;
+  const int vdec = (LEAN == 1 || LEAN == 3) ? 0 : LEAN == 2 ? 4 : LEAN == 4 ? 2 : p.vdec;
   // LEAN 2: the four levels of the 2-bit codes split into fp16 heads and
   // fp16 remainders (level = head + remainder to ~2^-22), as byte-permute
   // sources: low bytes of levels 0..3 in *_lo, high bytes in *_hi
@@ -795,7 +795,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
   const uint2* hqs = reinterpret_cast<const uint2*>(&ms.qc[0][0]);
   bool heavy_mma = false;
 
-  if (!LEAN && p.vfmt == SS_V_VQ) {
+  if ((!LEAN || LEAN == 4) && p.vfmt == SS_V_VQ) {
     // value centroids, once per CTA: [v_nb][256][v_bd] fp16 with entries
     // c >= v_k zeroed, so any stored index byte reads a finite row (the
     // unit loop's first barrier publishes the table)
@@ -1947,6 +1947,13 @@ int launch_decode(const DecodeParams& p, const CUtensorMap& mv, const CUtensorMa
       if (nb16 && hv && p.vdec == 0 && p.n_tt == 0 && !p.causal && p.mask == nullptr && cw == 8)
         kern = decode_attn_kernel<R, D, 16, 8, kHv, 3>;
     }
+  }
+  // block-VQ values (both K and V as block VQ, the model harness's cache),
+  // compressed tokens only, no heavy blocks, no masks
+  if constexpr ((R == 2 || R == 4) && D == 128) {
+    if (!nb16 && p.vdec == 2 && p.n_heavy == 0 && p.n_tt == 0 && !p.causal && p.mask == nullptr &&
+        cw == 8)
+      kern = decode_attn_kernel<R, D, 0, 8, false, 4>;
   }
   if (cw == 16 && !lean16)
     return fail(SS_ERR_UNSUPPORTED, "ss_decode_attn: 16 consumer warps need the lean 2-bit kernel");
