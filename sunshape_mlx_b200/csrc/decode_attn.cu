@@ -1639,7 +1639,29 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
         named_bar_sync(1, (CW * 32));
       }
     }
-    if (do_final) {
+    // fp16 output rows without a value rotation, 16-byte aligned: 8 elements
+    // per thread in one 16-byte store (fewer, larger writes, which matters
+    // when the output lives in page-locked host memory)
+    const bool vec_out = do_final && !p.part_out && !p.v_rot && p.odt == SS_F16 &&
+                         (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 &&
+                         ((p.o_sb | p.o_sh | p.o_st) & 7) == 0;
+    if (vec_out) {
+      for (int e8 = ctid; e8 < R * D / 8; e8 += (CW * 32)) {
+        const int r = e8 / (D / 8), j0 = (e8 - r * (D / 8)) * 8;
+        const int rr = rg * R + r;
+        if (rr >= rows_valid) continue;
+        const int rep = rr / p.tq, tqi = rr - rep * p.tq;
+        const int qh = hh * p.nrep + rep;
+        const float inv = ms.lrow[r] > 0.f ? 1.f / ms.lrow[r] : 0.f;
+        uint4 h;
+        h.x = pack_h2(mo[r][j0] * inv, mo[r][j0 + 1] * inv);
+        h.y = pack_h2(mo[r][j0 + 2] * inv, mo[r][j0 + 3] * inv);
+        h.z = pack_h2(mo[r][j0 + 4] * inv, mo[r][j0 + 5] * inv);
+        h.w = pack_h2(mo[r][j0 + 6] * inv, mo[r][j0 + 7] * inv);
+        *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(p.out) + bb * p.o_sb + qh * p.o_sh +
+                                  tqi * p.o_st + j0) = h;
+      }
+    } else if (do_final) {
       for (int e = ctid; e < R * D; e += (CW * 32)) {
         const int r = e / D, j = e - r * D;
         const int rr = rg * R + r;
