@@ -181,13 +181,6 @@ __device__ __forceinline__ uint32_t kmaj_off(int row, int kel, int kt) {
   return (uint32_t)((row >> 3) * (kt * 16) + (kel >> 3) * 128 + (row & 7) * 16 + (kel & 7) * 2);
 }
 
-struct Bar {
-  uint64_t* a_full;   // [slots] producers -> MMA (128 arrivals)
-  uint64_t* a_empty;  // [slots] epilogue group -> producers (4 arrivals)
-  uint64_t* t_full;   // [2] MMA commit -> epilogue group
-  uint64_t* t_empty;  // [2] epilogue group -> MMA (4 arrivals)
-};
-
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                                         const TcParams& p) {
   if (mbar_try_wait(bar, parity)) return true;
