@@ -1268,27 +1268,25 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
           ldsm_x2_trans(pw_perm + ks * 256, bp0, bp1);
           if constexpr (R == 8) ldsm_x2_trans(pwl_perm + ks * 256, cp0, cp1);
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            uint32_t w[2][2][4];  // [token pair][first, second token][word]
+          for (int qg = 0; qg < 4; ++qg) {  // scale group qg: m-tiles 2 qg, 2 qg + 1
+            uint32_t w[2][2][2];  // [token pair][first, second token][word]
 #pragma unroll
             for (int pr = 0; pr < 2; ++pr)
 #pragma unroll
               for (int e = 0; e < 2; ++e) {
-                const uint32_t wa = sbase + (uint32_t)(tok + 8 * pr + 4 * e) * 32u + half * 16u;
-                asm("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-                    : "=r"(w[pr][e][0]), "=r"(w[pr][e][1]), "=r"(w[pr][e][2]), "=r"(w[pr][e][3])
-                    : "r"(wa));
+                const uint32_t wa = sbase + (uint32_t)(tok + 8 * pr + 4 * e) * 32u + qg * 8u;
+                asm("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(w[pr][e][0]), "=r"(w[pr][e][1]) : "r"(wa));
               }
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int mt = half * 4 + i;
+            for (int i = 0; i < 2; ++i) {
+              const int mt = 2 * qg + i;
               uint32_t fr[2][2];  // [token pair][dim g, dim g + 8]
 #pragma unroll
               for (int pr = 0; pr < 2; ++pr) {
                 const uint32_t z = __byte_perm(w[pr][0][i], w[pr][1][i], zsel);
                 const uint32_t c4 = (z >> csh) & 0x03030303u;
                 const uint32_t sel = c4 * 0x11u + 0x40404040u;
-                const uint32_t sc = sc2[pr][mt >> 1];
+                const uint32_t sc = sc2[pr][qg];
 #pragma unroll
                 for (int d8 = 0; d8 < 2; ++d8) {
                   const uint32_t sl = d8 ? sel >> 16 : sel;
@@ -1301,8 +1299,8 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) decode_attn_kernel(
                   asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(fr[pr][d8]) : "r"(h), "r"(sc), "r"(ls));
                 }
               }
-              // a0 (dim g, tokens 2t..), a1 (dim g+8, tokens 2t..), a2 (dim g,
-              // tokens 2t+8..), a3 (dim g+8, tokens 2t+8..)
+              // a0 (dim g, slots 2t, 2t+1), a1 (dim g+8, same slots), a2 (dim
+              // g, slots 2t+8, 2t+9), a3 (dim g+8, same slots)
               if constexpr (R == 8) mma_16816(acc[mt], fr[0][0], fr[0][1], fr[1][0], fr[1][1], cp0, cp1);
               mma_16816(acc[mt], fr[0][0], fr[0][1], fr[1][0], fr[1][1], bp0, bp1);
             }
